@@ -1,0 +1,241 @@
+"""CPU oracle, Python face. TEST INFRASTRUCTURE ONLY.
+
+The parity tests, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
+``bench.py`` call this as the checker. The product (the CUDA library under
+``llm-kv260_b200/``) never imports it.
+
+The functions mirror the reference contract ``src/llm_kv260/q4_0.py`` name for
+name, with the same argument meaning and the same errors (TypeError for a wrong
+dtype, ValueError for a wrong shape), and run the C restatement in
+``q4_0_oracle.c`` through ctypes. The rank-ordered sum restates
+``board/tp/tp_llama.cpp:515-521``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+QK = 32            # q4_0.py:59
+Q4_0_BYTES = 18    # q4_0.py:60
+Q8_0_BYTES = 34    # q4_0.py:61
+LANES = 8          # q4_0.py:62
+CONTRACT_VERSION = "llm-kv260/w4a8-q4_0-v2"   # q4_0.py:64
+
+ROUND_CONTRACT = 0   # floor(|s| + 0.5f) with sign, q4_0.py:96
+ROUND_ROUNDF = 1     # roundf, tp_llama.cpp:343 (vcvtaq)
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle_q4.so")
+_lib = None
+
+
+def build(force: bool = False) -> str:
+    """Compile the C restatement with its Makefile (gcc, -ffp-contract=off)."""
+    src = os.path.join(_HERE, "q4_0_oracle.c")
+    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+        subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        P, I64, I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+        sig = {
+            "oracle_f32_to_f16": (ctypes.c_uint16, [ctypes.c_float]),
+            "oracle_f16_to_f32": (ctypes.c_float, [ctypes.c_uint16]),
+            "oracle_tree_sum8": (ctypes.c_float, [P]),
+            "oracle_quantize_q8_0": (I, [P, I64, P, P, I]),
+            "oracle_quantize_q4_0": (I, [P, I64, I64, P, I]),
+            "oracle_unpack_q4_0": (I, [P, I64, I64, P, P]),
+            "oracle_dequantize_q4_0": (I, [P, I64, I64, P]),
+            "oracle_gemv_q4_0": (I, [P, I64, I64, P, P, P, I, I]),
+            "oracle_gemv_q4_0_f32": (I, [P, I64, I64, P, P, I, I]),
+            "oracle_pack_x_for_engine": (I, [P, P, I64, P]),
+            "oracle_gemv_q4_0_packed": (I, [P, I64, I64, P, P, I]),
+            "oracle_gemv2_chunk_offset": (I64, [I, I, I, I, ctypes.POINTER(ctypes.c_int)]),
+            "oracle_allreduce_ordered": (I, [P, I, I64, P]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = L
+    return _lib
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def _check(rc: int, what: str) -> None:
+    if rc == -1:
+        raise ValueError(f"{what}: shape rejected by the contract")
+    if rc != 0:
+        raise RuntimeError(f"{what}: oracle returned {rc}")
+
+
+def default_threads() -> int:
+    return max(1, len(os.sched_getaffinity(0)))
+
+
+# ------------------------------------------------------------- float16 / tree
+
+def f32_to_f16_bits(v: float) -> int:
+    return int(lib().oracle_f32_to_f16(ctypes.c_float(v)))
+
+
+def f16_bits_to_f32(h: int) -> float:
+    return float(lib().oracle_f16_to_f32(ctypes.c_uint16(h)))
+
+
+def tree_sum(values: np.ndarray) -> np.ndarray:
+    """q4_0.py:67-78 for the 8-lane case the contract uses (last axis 8)."""
+    values = np.ascontiguousarray(values, dtype=np.float32)
+    if values.shape[-1] != LANES:
+        raise ValueError(f"the oracle's tree is over {LANES} lanes, got {values.shape[-1]}")
+    flat = values.reshape(-1, LANES)
+    out = np.empty(flat.shape[0], dtype=np.float32)
+    for i in range(flat.shape[0]):
+        out[i] = lib().oracle_tree_sum8(_ptr(np.ascontiguousarray(flat[i])))
+    return out.reshape(values.shape[:-1])
+
+
+# ------------------------------------------------------------------ quantizers
+
+def quantize_q8_0(x: np.ndarray, round_mode: int = ROUND_CONTRACT) -> tuple[np.ndarray, np.ndarray]:
+    """q4_0.py:83-97. Returns (q int8 [K], d float16 [K/32])."""
+    if x.dtype != np.float32:
+        raise TypeError(f"activations must be float32, got {x.dtype}")
+    if x.ndim != 1 or x.shape[0] % QK:
+        raise ValueError(f"x must be 1-D with a multiple of {QK} elements, got {x.shape}")
+    x = np.ascontiguousarray(x)
+    q = np.empty(x.shape[0], dtype=np.int8)
+    d = np.empty(x.shape[0] // QK, dtype=np.uint16)
+    _check(lib().oracle_quantize_q8_0(_ptr(x), x.shape[0], _ptr(q), _ptr(d), round_mode), "quantize_q8_0")
+    return q, d.view(np.float16)
+
+
+def quantize_q4_0(w: np.ndarray, threads: int | None = None) -> np.ndarray:
+    """q4_0.py:100-121. Returns uint8 [N, K/32*18]."""
+    if w.dtype != np.float32:
+        raise TypeError(f"weights must be float32, got {w.dtype}")
+    n, k = w.shape
+    if k % QK:
+        raise ValueError(f"in_features must be a multiple of {QK}, got {k}")
+    w = np.ascontiguousarray(w)
+    out = np.empty((n, k // QK * Q4_0_BYTES), dtype=np.uint8)
+    _check(lib().oracle_quantize_q4_0(_ptr(w), n, k, _ptr(out), threads or default_threads()), "quantize_q4_0")
+    return out
+
+
+# ----------------------------------------------------------------------- codec
+
+def unpack_q4_0(blocks: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """q4_0.py:126-140."""
+    if blocks.dtype != np.uint8:
+        raise TypeError(f"expected uint8 block bytes, got {blocks.dtype}")
+    n = blocks.shape[0]
+    nb = k // QK
+    if blocks.shape[1] != nb * Q4_0_BYTES:
+        raise ValueError(f"{blocks.shape[1]} bytes per row is not {nb} blocks of {Q4_0_BYTES}")
+    blocks = np.ascontiguousarray(blocks)
+    ints = np.empty((n, k), dtype=np.int8)
+    d = np.empty((n, nb), dtype=np.uint16)
+    _check(lib().oracle_unpack_q4_0(_ptr(blocks), n, k, _ptr(ints), _ptr(d)), "unpack_q4_0")
+    return ints, d.view(np.float16)
+
+
+def dequantize_q4_0(blocks: np.ndarray, k: int) -> np.ndarray:
+    """q4_0.py:143-146."""
+    if blocks.dtype != np.uint8:
+        raise TypeError(f"expected uint8 block bytes, got {blocks.dtype}")
+    n = blocks.shape[0]
+    if blocks.shape[1] != k // QK * Q4_0_BYTES:
+        raise ValueError("row byte count does not match k")
+    blocks = np.ascontiguousarray(blocks)
+    out = np.empty((n, k), dtype=np.float32)
+    _check(lib().oracle_dequantize_q4_0(_ptr(blocks), n, k, _ptr(out)), "dequantize_q4_0")
+    return out
+
+
+# ------------------------------------------------------------------------ gemv
+
+def gemv_q4_0(blocks: np.ndarray, k: int, xq: np.ndarray, xd: np.ndarray,
+              threads: int | None = None, allow_ragged_lanes: bool = False) -> np.ndarray:
+    """q4_0.py:151-182: float32 [N] in the engine's order."""
+    if xq.dtype != np.int8 or xd.dtype != np.float16:
+        raise TypeError(f"x must be (int8, float16), got ({xq.dtype}, {xd.dtype})")
+    if blocks.dtype != np.uint8:
+        raise TypeError(f"expected uint8 block bytes, got {blocks.dtype}")
+    n = blocks.shape[0]
+    nb = k // QK
+    if k % QK or blocks.shape[1] != nb * Q4_0_BYTES:
+        raise ValueError(f"{blocks.shape[1]} bytes per row is not {nb} blocks of {Q4_0_BYTES}")
+    if xq.shape != (k,) or xd.shape != (nb,):
+        raise ValueError(f"x shapes {xq.shape}, {xd.shape} do not match K={k}")
+    if nb % LANES and not allow_ragged_lanes:
+        raise ValueError(f"{nb} blocks is not a multiple of {LANES} lanes")
+    blocks = np.ascontiguousarray(blocks)
+    xq = np.ascontiguousarray(xq)
+    xd16 = np.ascontiguousarray(xd).view(np.uint16)
+    y = np.empty(n, dtype=np.float32)
+    _check(lib().oracle_gemv_q4_0(_ptr(blocks), n, k, _ptr(xq), _ptr(xd16), _ptr(y),
+                                  threads or default_threads(), int(allow_ragged_lanes)), "gemv_q4_0")
+    return y
+
+
+def gemv_q4_0_f32(blocks: np.ndarray, k: int, x: np.ndarray, threads: int | None = None,
+                  round_mode: int = ROUND_CONTRACT) -> np.ndarray:
+    """q4_0.py:185-188."""
+    xq, xd = quantize_q8_0(x, round_mode)
+    return gemv_q4_0(blocks, k, xq, xd, threads)
+
+
+def pack_x_for_engine(xq: np.ndarray, xd: np.ndarray) -> np.ndarray:
+    """q4_0.py:193-200: int8[K] then float32[K/32]."""
+    k = xq.shape[0]
+    out = np.empty(k + 4 * (k // QK), dtype=np.uint8)
+    _check(lib().oracle_pack_x_for_engine(_ptr(np.ascontiguousarray(xq)),
+                                          _ptr(np.ascontiguousarray(xd).view(np.uint16)), k, _ptr(out)),
+           "pack_x_for_engine")
+    return out
+
+
+def gemv_q4_0_packed(blocks: np.ndarray, k: int, xpacked: np.ndarray, threads: int | None = None) -> np.ndarray:
+    """The GEMV over the engine's activation buffer (board/kv260gemv/gemv_dev.h:19-23)."""
+    n = blocks.shape[0]
+    if xpacked.dtype != np.uint8 or xpacked.shape != (k + 4 * (k // QK),):
+        raise ValueError("xpacked must be uint8[k + 4*k/32]")
+    y = np.empty(n, dtype=np.float32)
+    _check(lib().oracle_gemv_q4_0_packed(_ptr(np.ascontiguousarray(blocks)), n, k,
+                                         _ptr(np.ascontiguousarray(xpacked)), _ptr(y),
+                                         threads or default_threads()), "gemv_q4_0_packed")
+    return y
+
+
+def gemv2_chunk_offset(r: int, c: int, rows: int, k: int) -> tuple[int, int]:
+    """board/kv260gemv/gemv2_dev.h:66-72. Returns (byte offset, port)."""
+    port = ctypes.c_int(0)
+    off = lib().oracle_gemv2_chunk_offset(r, c, rows, k, ctypes.byref(port))
+    return int(off), int(port.value)
+
+
+def allreduce_ordered(partials: list[np.ndarray]) -> np.ndarray:
+    """tp_llama.cpp:515-521: p0 + p1 + ... + p{n-1}, left to right, per element."""
+    parts = [np.ascontiguousarray(p, dtype=np.float32) for p in partials]
+    n = len(parts)
+    length = parts[0].shape[0]
+    if any(p.shape != (length,) for p in parts):
+        raise ValueError("partials must share one 1-D shape")
+    ptrs = (ctypes.c_void_p * n)(*[_ptr(p) for p in parts])
+    out = np.empty(length, dtype=np.float32)
+    _check(lib().oracle_allreduce_ordered(ctypes.cast(ptrs, ctypes.c_void_p), n, length, _ptr(out)),
+           "allreduce_ordered")
+    return out
