@@ -1,0 +1,15 @@
+"""llm-kv260 on B200: the Q4_0 x Q8_0 GEMV and the rank-ordered fp32
+all-reduce of al-nafisah/llm-kv260's decode hot path, as sm_100a kernels
+behind a C ABI (include/*.h) shaped like the reference's board/kv260gemv.
+
+The directory name has a hyphen, so it is loaded by path as module
+``llm_kv260_b200`` (``__graft_entry__.load_package()``).
+"""
+
+from __future__ import annotations
+
+from . import capi
+from .capi import B200Error, lib
+from .engine import Engine, Gemv2Dev, GemvDev, QMat, Udmabuf, dev_ptr
+
+__all__ = ["B200Error", "Engine", "Gemv2Dev", "GemvDev", "QMat", "Udmabuf", "capi", "dev_ptr", "lib"]

@@ -1,0 +1,125 @@
+"""ctypes declarations of the C ABI in include/*.h (libb200gemv.so).
+
+The library is required: if it is not built, `lib()` raises. There is no CPU
+path behind this module.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libb200gemv.so")
+
+c_int, c_uint, c_u64, c_size, c_vp, c_char_p = (ctypes.c_int, ctypes.c_uint, ctypes.c_uint64, ctypes.c_size_t,
+                                                 ctypes.c_void_p, ctypes.c_char_p)
+
+
+class gemv_dev_t(ctypes.Structure):
+    """include/gemv_dev.h"""
+    _fields_ = [("fd", c_int), ("stream", c_vp), ("done", c_vp), ("pending", c_int), ("owns_stream", c_int),
+                ("timeout_ms", c_int), ("started_ns", c_u64)]
+
+
+class gemv2_dev_t(ctypes.Structure):
+    """include/gemv2_dev.h"""
+    _fields_ = [("fetch", gemv_dev_t), ("mac", gemv_dev_t), ("w", c_u64 * 4), ("k", c_int), ("rows", c_int),
+                ("fetched", c_int)]
+
+
+class udmabuf_t(ctypes.Structure):
+    """include/udmabuf.h"""
+    _fields_ = [("fd", c_int), ("base", ctypes.POINTER(ctypes.c_uint8)), ("phys", c_u64), ("size", c_size),
+                ("used", c_size)]
+
+
+class b200_qmat_t(ctypes.Structure):
+    """include/b200_engine.h"""
+    _fields_ = [("w", c_u64), ("rows", c_int), ("k", c_int)]
+
+
+class b200_engine_config_t(ctypes.Structure):
+    """include/b200_engine.h"""
+    _fields_ = [("stage_bytes", c_int), ("stages", c_int), ("ctas_per_sm", c_int), ("l2_policy", c_int),
+                ("pdl", c_int), ("round_mode", c_int), ("fuse_quantize", c_int), ("prefetch_next", c_int)]
+
+
+P = ctypes.POINTER
+SIGNATURES: dict[str, tuple] = {
+    # gemv_dev.h
+    "gemv_dev_open": (c_int, [P(gemv_dev_t)]),
+    "gemv_dev_open_named": (c_int, [P(gemv_dev_t), c_char_p, c_int]),
+    "gemv_dev_close": (c_int, [P(gemv_dev_t)]),
+    "gemv_dev_run": (c_int, [P(gemv_dev_t), c_u64, c_u64, c_u64, c_int, c_int]),
+    "gemv_dev_start": (c_int, [P(gemv_dev_t), c_u64, c_u64, c_u64, c_int, c_int]),
+    "gemv_dev_wait": (c_int, [P(gemv_dev_t)]),
+    "gemv_dev_start4": (c_int, [P(gemv_dev_t), P(c_u64), c_u64, c_u64, c_int, c_int]),
+    "gemv_dev_set_stream": (c_int, [P(gemv_dev_t), c_vp]),
+    "gemv_dev_status": (c_int, [P(gemv_dev_t), P(c_uint)]),
+    "gemv_dev_last_error": (c_char_p, []),
+    # gemv2_dev.h
+    "gemv2_dev_open": (c_int, [P(gemv2_dev_t)]),
+    "gemv2_dev_close": (c_int, [P(gemv2_dev_t)]),
+    "gemv2_fetch_start": (c_int, [P(gemv2_dev_t), P(c_u64), c_int, c_int]),
+    "gemv2_fetch_wait": (c_int, [P(gemv2_dev_t)]),
+    "gemv2_mac_start": (c_int, [P(gemv2_dev_t), c_u64, c_u64, c_int, c_int]),
+    "gemv2_mac_wait": (c_int, [P(gemv2_dev_t)]),
+    "gemv2_mac_idle": (c_int, [P(gemv2_dev_t)]),
+    "gemv2_drain": (c_int, [P(gemv2_dev_t)]),
+    # udmabuf.h
+    "udmabuf_open": (c_int, [P(udmabuf_t), c_char_p]),
+    "udmabuf_open_size": (c_int, [P(udmabuf_t), c_char_p, c_size, c_int]),
+    "udmabuf_close": (c_int, [P(udmabuf_t)]),
+    "udmabuf_alloc": (c_vp, [P(udmabuf_t), c_size, c_size]),
+    "udmabuf_clean": (c_int, [c_vp, c_size]),
+    "udmabuf_invalidate": (c_int, [c_vp, c_size]),
+    # b200_engine.h
+    "b200_engine_open": (c_int, [P(c_vp), c_int]),
+    "b200_engine_close": (c_int, [c_vp]),
+    "b200_engine_get_config": (c_int, [c_vp, P(b200_engine_config_t)]),
+    "b200_engine_set_config": (c_int, [c_vp, P(b200_engine_config_t)]),
+    "b200_engine_set_stream": (c_int, [c_vp, c_vp]),
+    "b200_engine_stream": (c_vp, [c_vp]),
+    "b200_gemv_f32": (c_int, [c_vp, P(b200_qmat_t), c_u64, c_u64, P(b200_qmat_t)]),
+    "b200_gemv_q8": (c_int, [c_vp, P(b200_qmat_t), c_u64, c_u64, P(b200_qmat_t)]),
+    "b200_quantize_q8_0": (c_int, [c_vp, c_u64, c_u64, c_int]),
+    "b200_prefetch": (c_int, [c_vp, P(b200_qmat_t)]),
+    "b200_engine_sync": (c_int, [c_vp, c_int]),
+    "b200_engine_status": (c_int, [c_vp, P(c_uint)]),
+    "b200_gemv_plan": (c_int, [c_vp, c_int, c_int, c_int, P(c_int), P(c_int)]),
+    "b200_device_count": (c_int, []),
+    "b200_last_error": (c_char_p, []),
+}
+
+_lib: ctypes.CDLL | None = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load libb200gemv.so (built by llm-kv260_b200/build.py). Raises if absent."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is not built: run __graft_entry__.build() "
+                               "(there is no CPU fallback for the GEMV)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = L
+    return _lib
+
+
+class B200Error(RuntimeError):
+    """A C-ABI call returned a negative errno value."""
+
+    def __init__(self, what: str, code: int):
+        msg = lib().b200_last_error() or b""
+        super().__init__(f"{what} failed ({code}): {msg.decode(errors='replace')}")
+        self.code = code
+
+
+def check(rc: int, what: str) -> int:
+    if rc < 0:
+        raise B200Error(what, rc)
+    return rc

@@ -1,0 +1,83 @@
+// Internal host-side interface of the Q4_0 x Q8_0 GEMV kernels (not part of
+// the C ABI; the entry points in capi.cu call these).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace b200 {
+
+constexpr int kQK = 32;          // weights per block (q4_0.py:59)
+constexpr int kBlockBytes = 18;  // fp16 scale + 16 nibble bytes (q4_0.py:60)
+constexpr int kLanes = 8;        // q4_0.py:62
+constexpr int kChunkBytes = 144; // 8 blocks = 9 x 16 bytes (gemv2_dev.h:61)
+constexpr int kMaxK = 8192;      // x held in registers: 8 blocks per thread at most
+
+// Where the weight bytes are and how they are laid out.
+//   ROWS:  GGUF row-major Q4_0 rows (gemv_dev.h:19-21), split over 1 or 4
+//          regions of rows/nregions rows each (gemv_dev.h:29-35).
+//   PAIRS: the gemv2 interleave (gemv2_dev.h:46-49,66-72): 4 regions; inside
+//          a region row i pairs with row i + rows/8 and their 144-byte chunks
+//          alternate.
+enum Layout : int { kLayoutRows = 0, kLayoutPairs = 1 };
+
+// What x is.
+//   PACKED: the engine's buffer, int8[k] then float32[k/32] (q4_0.py:193-200).
+//   F32:    float32[k], quantised to Q8_0 inside the kernel (q4_0.py:185-188).
+enum XMode : int { kXPacked = 0, kXF32 = 1 };
+
+enum RoundMode : int { kRoundContract = 0, kRoundRoundf = 1 };
+
+// L2 policy for the streamed weight bytes.
+enum L2Policy : int { kL2EvictFirst = 0, kL2EvictNormal = 1, kL2EvictLast = 2 };
+
+// Device status bits (a word per device, read with read_status()).
+enum Status : unsigned { kStatusOk = 0, kStatusStageTimeout = 1u, kStatusPeerTimeout = 2u };
+
+struct GemvLaunch {
+    const uint8_t *region[4] = {nullptr, nullptr, nullptr, nullptr};
+    int nregions = 1;
+    int rows = 0;
+    int k = 0;
+    int layout = kLayoutRows;
+    int xmode = kXPacked;
+    const void *x = nullptr;
+    float *y = nullptr;
+    int round_mode = kRoundContract;
+    int l2_policy = kL2EvictFirst;
+    bool pdl = false;  // launch with programmatic stream serialisation
+};
+
+struct Tuning {
+    int stage_bytes = 16384;  // target bytes per pipeline stage
+    int stages = 4;           // stages in flight per CTA
+    int ctas_per_sm = 2;      // grid = SMs x this, at most one CTA per stage
+};
+
+// Error codes shared with the C ABI (negative errno values).
+constexpr int kErrInval = -22;   // -EINVAL
+constexpr int kErrNoDev = -19;   // -ENODEV
+constexpr int kErrTimeout = -110;  // -ETIMEDOUT
+constexpr int kErrBusy = -16;    // -EBUSY
+constexpr int kErrCuda = -5;     // -EIO: a CUDA call failed
+constexpr int kErrNoMem = -12;   // -ENOMEM
+
+// Checks shapes and alignment; returns 0 or kErrInval with *why set.
+int gemv_validate(const GemvLaunch &L, const char **why);
+int gemv_launch(const GemvLaunch &L, const Tuning &tu, cudaStream_t stream);
+
+// x float32[k] -> engine buffer int8[k] + float32[k/32] (quantize_q8_0 + pack_x_for_engine).
+int quantize_launch(const float *x, uint8_t *xpacked, int k, int round_mode, cudaStream_t stream, bool pdl);
+
+// Pull `bytes` bytes at each region start into L2 (gemv2's fetch-ahead).
+int prefetch_l2_launch(const uint8_t *const *region, int nregions, size_t bytes_per_region, cudaStream_t stream);
+
+int read_status(unsigned *status);   // device status word of the current device
+int clear_status();
+
+// Grid the GEMV would launch (for the bench's roofline accounting).
+int gemv_grid(const GemvLaunch &L, const Tuning &tu, int *grid, int *smem_bytes);
+
+}  // namespace b200
