@@ -29,11 +29,21 @@ typedef struct b200_engine b200_engine_t;
 
 /* A Q4_0 matrix in device memory: replaces qmat (tp_llama.cpp:105-119), one
  * region instead of four staggered port quarters (HBM has no DDR-bank
- * collisions to dodge). */
+ * collisions to dodge). Two layouts:
+ *   B200_LAYOUT_ROWS   the GGUF bytes as they are: rows of k/32 18-byte blocks;
+ *   B200_LAYOUT_TILES  the engine's re-laid form (b200_repack_q4_0), which the
+ *                      fast kernel reads; the same 18 bytes per 32 weights, rows
+ *                      padded to a multiple of 16 (b200_tiled_bytes).
+ * The reference re-lays its weights at load in the same way for its own
+ * engine (tp_llama.cpp:102-118, the gemv2 chunk interleave). */
+#define B200_LAYOUT_ROWS 0
+#define B200_LAYOUT_TILES 1
+
 typedef struct {
-    uint64_t w;  /* first byte of row 0; rows are k/32*18 bytes apart */
+    uint64_t w;  /* first byte of the matrix, 16-byte aligned */
     int rows;
     int k;
+    int layout;  /* B200_LAYOUT_ROWS or B200_LAYOUT_TILES */
 } b200_qmat_t;
 
 typedef struct {
@@ -45,6 +55,7 @@ typedef struct {
     int round_mode;      /* Q8_0 rounding: 0 floor(|s|+0.5f) as q4_0.py:96 (default), 1 roundf as tp_llama.cpp:343 */
     int fuse_quantize;   /* b200_gemv_f32: 1 quantise inside each GEMV CTA, 0 a separate quantise kernel (default 0) */
     int prefetch_next;   /* 1: a `next` hint issues an L2 prefetch of that matrix on a side stream (default 0) */
+    int xreg_chunks;     /* rows of at most this many 144-byte chunks (K <= 256*this, at most 8) keep x in registers (default 8) */
 } b200_engine_config_t;
 
 /* Replaces engine_t::probe + engine_t::open (tp_llama.cpp:303-317). */
@@ -69,12 +80,38 @@ B200_API int b200_quantize_q8_0(b200_engine_t *e, uint64_t x, uint64_t xpacked, 
 /* Replaces engine_t::prefetch (tp_llama.cpp:318-323): L2 prefetch of W. */
 B200_API int b200_prefetch(b200_engine_t *e, const b200_qmat_t *W);
 
+/* Bytes of the tile layout of a rows x k matrix (0 for an unusable shape). */
+B200_API uint64_t b200_tiled_bytes(int rows, int k);
+/* Re-lay GGUF Q4_0 rows at `src` (2-byte aligned) into tiles at `dst`
+ * (16-byte aligned, b200_tiled_bytes(rows, k) bytes) on the engine's stream. */
+B200_API int b200_repack_q4_0(b200_engine_t *e, uint64_t src, int rows, int k, uint64_t dst);
+
+/* Greedy pick over y[0..n) on the device, as the runtime's scan does
+ * (tp_llama.cpp:879-882: first index of the largest value): writes the
+ * int32 index + index_base, then the float32 value, to the 8 bytes at `out`. */
+B200_API int b200_argmax_f32(b200_engine_t *e, uint64_t y, int n, int index_base, uint64_t out);
+
+/* Graphs: record a sequence of engine calls once and replay it with one
+ * launch (a decode token is ~70 dependent kernels; replaying them as a CUDA
+ * graph with programmatic dependent launch removes the per-kernel CPU cost).
+ * Between capture_begin and capture_end the engine's calls are recorded, not
+ * run; run every call once before capturing it (first calls set up caches).
+ * The engine must be on a stream of its own (not the legacy default). */
+typedef struct b200_graph b200_graph_t;
+B200_API int b200_capture_begin(b200_engine_t *e);
+B200_API int b200_capture_end(b200_engine_t *e, b200_graph_t **g);
+B200_API int b200_graph_launch(b200_engine_t *e, b200_graph_t *g);
+B200_API int b200_graph_destroy(b200_graph_t *g);
+/* Asynchronous copy of `bytes` bytes on the engine's stream, any direction
+ * (unified addressing); host memory should be pinned. */
+B200_API int b200_copy_async(b200_engine_t *e, uint64_t dst, uint64_t src, uint64_t bytes);
+
 /* Block until the engine's queued work is done (bounded; -ETIMEDOUT). */
 B200_API int b200_engine_sync(b200_engine_t *e, int timeout_ms);
 /* Device status word (see gemv_dev_status); reading clears it. */
 B200_API int b200_engine_status(b200_engine_t *e, unsigned *status);
 /* Launch shape the GEMV would use for W (for roofline accounting). */
-B200_API int b200_gemv_plan(b200_engine_t *e, int rows, int k, int fused_f32, int *grid, int *smem_bytes);
+B200_API int b200_gemv_plan(b200_engine_t *e, int rows, int k, int layout, int fused_f32, int *grid, int *smem_bytes);
 
 B200_API int b200_device_count(void);
 /* Message for the last error on this thread (never NULL). */

@@ -10,6 +10,7 @@ from __future__ import annotations
 
 from . import capi
 from .capi import B200Error, lib
-from .engine import Engine, Gemv2Dev, GemvDev, QMat, Udmabuf, dev_ptr
+from .engine import LAYOUT_ROWS, LAYOUT_TILES, Engine, Gemv2Dev, GemvDev, QMat, Udmabuf, dev_ptr, tiled_bytes
 
-__all__ = ["B200Error", "Engine", "Gemv2Dev", "GemvDev", "QMat", "Udmabuf", "capi", "dev_ptr", "lib"]
+__all__ = ["B200Error", "Engine", "Gemv2Dev", "GemvDev", "LAYOUT_ROWS", "LAYOUT_TILES", "QMat", "Udmabuf", "capi",
+           "dev_ptr", "lib", "tiled_bytes"]

@@ -469,6 +469,7 @@ struct b200_engine {
     cudaEvent_t fork;
     cudaEvent_t done;
     uint8_t *xscratch;  // quantised x for the two-kernel f32 path
+    void *sel_scratch;  // argmax candidates
     b200_engine_config_t cfg;
 };
 
@@ -481,25 +482,57 @@ Tuning tuning_of(const b200_engine_config_t &c) {
     t.stage_bytes = c.stage_bytes;
     t.stages = c.stages;
     t.ctas_per_sm = c.ctas_per_sm;
+    t.xreg_chunks = c.xreg_chunks;
     return t;
 }
 
-int qmat_launch(b200_engine_t *e, const b200_qmat_t *W, int xmode, const void *x, uint64_t y, GemvLaunch *L) {
+// One engine GEMV: validate, then launch the kernel of W's layout.
+int engine_gemv(b200_engine_t *e, const b200_qmat_t *W, int xmode, const void *x, uint64_t y) {
     if (!e) return fail(kErrInval, "engine not open");
     if (!W) return fail(kErrInval, "null matrix");
-    L->region[0] = reinterpret_cast<const uint8_t *>(W->w);
-    L->nregions = 1;
-    L->rows = W->rows;
-    L->k = W->k;
-    L->layout = kLayoutRows;
-    L->xmode = xmode;
-    L->x = x;
-    L->y = reinterpret_cast<float *>(y);
-    L->round_mode = e->cfg.round_mode;
-    L->l2_policy = e->cfg.l2_policy;
-    L->pdl = e->cfg.pdl != 0;
     const char *why = nullptr;
-    if (gemv_validate(*L, &why)) return fail(kErrInval, "gemv %dx%d: %s", W->rows, W->k, why);
+    if (W->layout == B200_LAYOUT_TILES) {
+        TileLaunch L;
+        L.w = reinterpret_cast<const uint8_t *>(W->w);
+        L.rows = W->rows;
+        L.k = W->k;
+        L.xmode = xmode;
+        L.x = x;
+        L.y = reinterpret_cast<float *>(y);
+        L.round_mode = e->cfg.round_mode;
+        L.l2_policy = e->cfg.l2_policy;
+        L.pdl = e->cfg.pdl != 0;
+        if (tile_validate(L, &why)) return fail(kErrInval, "gemv %dx%d: %s", W->rows, W->k, why);
+        if (int rc = use_device(e->device)) return rc;
+        if (tile_launch(L, tuning_of(e->cfg), e->stream))
+            return fail(kErrCuda, "gemv launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return 0;
+    }
+    if (W->layout != B200_LAYOUT_ROWS) return fail(kErrInval, "unknown matrix layout %d", W->layout);
+    GemvLaunch L;
+    L.region[0] = reinterpret_cast<const uint8_t *>(W->w);
+    L.nregions = 1;
+    L.rows = W->rows;
+    L.k = W->k;
+    L.layout = kLayoutRows;
+    L.xmode = xmode;
+    L.x = x;
+    L.y = reinterpret_cast<float *>(y);
+    L.round_mode = e->cfg.round_mode;
+    L.l2_policy = e->cfg.l2_policy;
+    L.pdl = e->cfg.pdl != 0;
+    if (gemv_validate(L, &why)) return fail(kErrInval, "gemv %dx%d: %s", W->rows, W->k, why);
+    if (int rc = use_device(e->device)) return rc;
+    if (gemv_launch(L, tuning_of(e->cfg), e->stream))
+        return fail(kErrCuda, "gemv launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return 0;
+}
+
+// Shape checks shared by the f32 path (before it quantises into scratch).
+int check_qmat(const b200_qmat_t *W) {
+    if (!W) return fail(kErrInval, "null matrix");
+    if (W->k <= 0 || W->k % 256 || W->k > kMaxK) return fail(kErrInval, "gemv %dx%d: k must be a multiple of 256 in [256, 8192]", W->rows, W->k);
+    if (W->rows <= 0) return fail(kErrInval, "gemv: rows must be positive");
     return 0;
 }
 
@@ -509,7 +542,8 @@ int prefetch_on_side(b200_engine_t *e, const b200_qmat_t *W) {
     if (err == cudaSuccess) err = cudaStreamWaitEvent(e->side, e->fork, 0);
     if (err != cudaSuccess) return cuda_fail(err, "prefetch fork");
     const uint8_t *r[1] = {reinterpret_cast<const uint8_t *>(W->w)};
-    const size_t bytes = static_cast<size_t>(W->rows) * (W->k / kQK) * kBlockBytes;
+    const size_t bytes = W->layout == B200_LAYOUT_TILES ? tiled_bytes(W->rows, W->k)
+                                                        : static_cast<size_t>(W->rows) * (W->k / kQK) * kBlockBytes;
     return prefetch_l2_launch(r, 1, bytes, e->side) ? fail(kErrCuda, "prefetch launch failed") : 0;
 }
 
@@ -537,6 +571,7 @@ extern "C" int b200_engine_open(b200_engine_t **out, int device) {
     if (err == cudaSuccess) err = cudaEventCreateWithFlags(&e->fork, cudaEventDisableTiming);
     if (err == cudaSuccess) err = cudaEventCreateWithFlags(&e->done, cudaEventDisableTiming);
     if (err == cudaSuccess) err = cudaMalloc(reinterpret_cast<void **>(&e->xscratch), kXScratchBytes);
+    if (err == cudaSuccess) err = cudaMalloc(&e->sel_scratch, static_cast<size_t>(argmax_scratch_bytes()));
     if (err != cudaSuccess) {
         b200_engine_close(e);
         return cuda_fail(err, "engine set-up");
@@ -550,6 +585,7 @@ extern "C" int b200_engine_open(b200_engine_t **out, int device) {
     e->cfg.round_mode = kRoundContract;
     e->cfg.fuse_quantize = 0;
     e->cfg.prefetch_next = 0;
+    e->cfg.xreg_chunks = 8;
     *out = e;
     return 0;
 }
@@ -560,6 +596,7 @@ extern "C" int b200_engine_close(b200_engine_t *e) {
     if (e->stream) cudaStreamSynchronize(e->stream);
     if (e->side) cudaStreamSynchronize(e->side);
     if (e->xscratch) cudaFree(e->xscratch);
+    if (e->sel_scratch) cudaFree(e->sel_scratch);
     if (e->fork) cudaEventDestroy(e->fork);
     if (e->done) cudaEventDestroy(e->done);
     if (e->side) cudaStreamDestroy(e->side);
@@ -605,11 +642,7 @@ extern "C" int b200_quantize_q8_0(b200_engine_t *e, uint64_t x, uint64_t xpacked
 
 extern "C" int b200_gemv_q8(b200_engine_t *e, const b200_qmat_t *W, uint64_t xpacked, uint64_t y,
                             const b200_qmat_t *next) {
-    GemvLaunch L;
-    if (int rc = qmat_launch(e, W, kXPacked, reinterpret_cast<const void *>(xpacked), y, &L)) return rc;
-    if (int rc = use_device(e->device)) return rc;
-    if (gemv_launch(L, tuning_of(e->cfg), e->stream))
-        return fail(kErrCuda, "gemv launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    if (int rc = engine_gemv(e, W, kXPacked, reinterpret_cast<const void *>(xpacked), y)) return rc;
     if (next && e->cfg.prefetch_next) return prefetch_on_side(e, next);
     return 0;
 }
@@ -617,22 +650,38 @@ extern "C" int b200_gemv_q8(b200_engine_t *e, const b200_qmat_t *W, uint64_t xpa
 extern "C" int b200_gemv_f32(b200_engine_t *e, const b200_qmat_t *W, uint64_t x, uint64_t y,
                              const b200_qmat_t *next) {
     if (!e) return fail(kErrInval, "engine not open");
-    GemvLaunch L;
+    if (int rc = check_qmat(W)) return rc;
     if (!e->cfg.fuse_quantize) {
-        // Validate the matrix first: the scratch buffer holds k <= 8192 only.
-        if (int rc = qmat_launch(e, W, kXPacked, e->xscratch, y, &L)) return rc;
+        // The scratch buffer holds k <= 8192, checked above.
         if (x % 16) return fail(kErrInval, "x must be 16-byte aligned");
         if (int rc = b200_quantize_q8_0(e, x, reinterpret_cast<uint64_t>(e->xscratch), W->k)) return rc;
-        if (gemv_launch(L, tuning_of(e->cfg), e->stream))
-            return fail(kErrCuda, "gemv launch failed: %s", cudaGetErrorString(cudaGetLastError()));
-        if (next && e->cfg.prefetch_next) return prefetch_on_side(e, next);
-        return 0;
+        return b200_gemv_q8(e, W, reinterpret_cast<uint64_t>(e->xscratch), y, next);
     }
-    if (int rc = qmat_launch(e, W, kXF32, reinterpret_cast<const void *>(x), y, &L)) return rc;
-    if (int rc = use_device(e->device)) return rc;
-    if (gemv_launch(L, tuning_of(e->cfg), e->stream))
-        return fail(kErrCuda, "gemv launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    if (int rc = engine_gemv(e, W, kXF32, reinterpret_cast<const void *>(x), y)) return rc;
     if (next && e->cfg.prefetch_next) return prefetch_on_side(e, next);
+    return 0;
+}
+
+extern "C" uint64_t b200_tiled_bytes(int rows, int k) { return static_cast<uint64_t>(tiled_bytes(rows, k)); }
+
+extern "C" int b200_repack_q4_0(b200_engine_t *e, uint64_t src, int rows, int k, uint64_t dst) {
+    if (!e) return fail(kErrInval, "engine not open");
+    if (tiled_bytes(rows, k) == 0) return fail(kErrInval, "repack %dx%d: k must be a multiple of 256", rows, k);
+    if (src % 2 || dst % 16) return fail(kErrInval, "repack: src must be 2-byte and dst 16-byte aligned");
+    if (int rc = use_device(e->device)) return rc;
+    if (repack_launch(reinterpret_cast<const uint8_t *>(src), rows, k, reinterpret_cast<uint8_t *>(dst), e->stream))
+        return fail(kErrCuda, "repack launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return 0;
+}
+
+extern "C" int b200_argmax_f32(b200_engine_t *e, uint64_t y, int n, int index_base, uint64_t out) {
+    if (!e) return fail(kErrInval, "engine not open");
+    if (!y || n <= 0 || !out || y % 4 || out % 4) return fail(kErrInval, "argmax: bad arguments");
+    if (int rc = use_device(e->device)) return rc;
+    int *oi = reinterpret_cast<int *>(out);
+    if (argmax_launch(reinterpret_cast<const float *>(y), n, index_base, e->sel_scratch, oi,
+                      reinterpret_cast<float *>(oi + 1), e->stream, e->cfg.pdl != 0))
+        return fail(kErrCuda, "argmax launch failed: %s", cudaGetErrorString(cudaGetLastError()));
     return 0;
 }
 
@@ -660,17 +709,97 @@ extern "C" int b200_engine_status(b200_engine_t *e, unsigned *status) {
     return clear_status() ? fail(kErrCuda, "status clear failed") : 0;
 }
 
-extern "C" int b200_gemv_plan(b200_engine_t *e, int rows, int k, int fused_f32, int *grid, int *smem_bytes) {
+extern "C" int b200_gemv_plan(b200_engine_t *e, int rows, int k, int layout, int fused_f32, int *grid,
+                              int *smem_bytes) {
     if (!e) return fail(kErrInval, "engine not open");
     if (int rc = use_device(e->device)) return rc;
-    GemvLaunch L;
     static const uint8_t aligned[16] __attribute__((aligned(16))) = {};
+    float *ydummy = reinterpret_cast<float *>(const_cast<uint8_t *>(aligned));
+    if (layout == B200_LAYOUT_TILES) {
+        TileLaunch L;
+        L.w = aligned;
+        L.rows = rows;
+        L.k = k;
+        L.xmode = fused_f32 ? kXF32 : kXPacked;
+        L.x = aligned;
+        L.y = ydummy;
+        if (int rc = tile_grid(L, tuning_of(e->cfg), grid, smem_bytes)) return fail(rc, "no plan for %dx%d", rows, k);
+        return 0;
+    }
+    GemvLaunch L;
     L.region[0] = aligned;
     L.rows = rows;
     L.k = k;
     L.xmode = fused_f32 ? kXF32 : kXPacked;
     L.x = aligned;
-    L.y = reinterpret_cast<float *>(const_cast<uint8_t *>(aligned));
+    L.y = ydummy;
     if (int rc = gemv_grid(L, tuning_of(e->cfg), grid, smem_bytes)) return fail(rc, "no plan for %dx%d", rows, k);
     return 0;
+}
+
+// ----------------------------------------------------------------- graphs
+
+struct b200_graph {
+    int device;
+    cudaGraph_t graph;
+    cudaGraphExec_t exec;
+};
+
+extern "C" int b200_capture_begin(b200_engine_t *e) {
+    if (!e) return fail(kErrInval, "engine not open");
+    if (int rc = use_device(e->device)) return rc;
+    if (e->stream == nullptr) return fail(kErrInval, "capture needs a stream of its own, not the legacy default");
+    const cudaError_t err = cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal);
+    return err == cudaSuccess ? 0 : cuda_fail(err, "cudaStreamBeginCapture");
+}
+
+extern "C" int b200_capture_end(b200_engine_t *e, b200_graph_t **g) {
+    if (!e || !g) return fail(kErrInval, "bad arguments");
+    *g = nullptr;
+    if (int rc = use_device(e->device)) return rc;
+    cudaGraph_t graph = nullptr;
+    cudaError_t err = cudaStreamEndCapture(e->stream, &graph);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaStreamEndCapture");
+    cudaGraphExec_t exec = nullptr;
+    err = cudaGraphInstantiate(&exec, graph, 0);
+    if (err != cudaSuccess) {
+        cudaGraphDestroy(graph);
+        return cuda_fail(err, "cudaGraphInstantiate");
+    }
+    b200_graph_t *out = static_cast<b200_graph_t *>(calloc(1, sizeof(b200_graph_t)));
+    if (!out) {
+        cudaGraphExecDestroy(exec);
+        cudaGraphDestroy(graph);
+        return fail(kErrNoMem, "out of host memory");
+    }
+    out->device = e->device;
+    out->graph = graph;
+    out->exec = exec;
+    *g = out;
+    return 0;
+}
+
+extern "C" int b200_graph_launch(b200_engine_t *e, b200_graph_t *g) {
+    if (!e || !g) return fail(kErrInval, "bad arguments");
+    if (g->device != e->device) return fail(kErrInval, "graph and engine are on different devices");
+    if (int rc = use_device(e->device)) return rc;
+    const cudaError_t err = cudaGraphLaunch(g->exec, e->stream);
+    return err == cudaSuccess ? 0 : cuda_fail(err, "cudaGraphLaunch");
+}
+
+extern "C" int b200_graph_destroy(b200_graph_t *g) {
+    if (!g) return 0;
+    use_device(g->device);
+    if (g->exec) cudaGraphExecDestroy(g->exec);
+    if (g->graph) cudaGraphDestroy(g->graph);
+    free(g);
+    return 0;
+}
+
+extern "C" int b200_copy_async(b200_engine_t *e, uint64_t dst, uint64_t src, uint64_t bytes) {
+    if (!e) return fail(kErrInval, "engine not open");
+    if (int rc = use_device(e->device)) return rc;
+    const cudaError_t err = cudaMemcpyAsync(reinterpret_cast<void *>(dst), reinterpret_cast<const void *>(src),
+                                            static_cast<size_t>(bytes), cudaMemcpyDefault, e->stream);
+    return err == cudaSuccess ? 0 : cuda_fail(err, "cudaMemcpyAsync");
 }

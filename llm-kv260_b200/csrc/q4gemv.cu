@@ -1,34 +1,40 @@
 // Q4_0 x Q8_0 GEMV for sm_100a, bit-exact to the reference contract
 // src/llm_kv260/q4_0.py (gemv_q4_0, lines 151-182).
 //
-// Data path (one CTA, 256 threads):
-//   * The CTA owns a contiguous range of weight units (a row, or a gemv2 row
-//     pair) inside one region. One elected thread streams that byte range into
-//     a ring of shared-memory stages with 1-D bulk copies (cp.async.bulk, the
-//     TMA engine) that complete on mbarriers, so each CTA keeps up to
-//     `stages` x ~16 KB in flight with no registers tied up in loads.
-//   * x is read once per CTA into registers: every thread always handles the
-//     same blocks b = t, t+T, t+2T, ... of every row, so its 8 int8x4 words,
-//     float32 scale and int sum per block stay in registers for all rows.
-//   * Each row is handled by a team of T = 8/16/32 threads. Thread t reads
-//     block b's 18 bytes from shared memory as five aligned 32-bit words and
-//     funnel-shifts the nibbles into place (the 2-byte misalignment of odd
-//     blocks is a per-thread constant), then computes the block dot with
-//     __dp4a: sumi = sum(nibble * x) - 8 * sum(x), exact in int32.
-//   * Float work follows the contract to the bit: t = (f32(sumi) * f32(dw)) *
-//     f32(dx) as two rounded multiplies; lane b mod 8 accumulates sequentially
-//     in b, which the team does by shuffling the (up to) four values a lane
-//     receives per T-block step to its owner thread and adding them in order;
-//     the final eight lanes go through xor-shuffles 1, 2, 4, which is exactly
-//     tree_sum's adjacent-pair tree (float addition is commutative).
-// Blocks past nb contribute +0.0f, an exact no-op on a lane that started at
-// +0.0f (a lane sum can never be -0.0f).
+// The contract's order fixes the parallel structure: block b of a row feeds
+// lane b mod 8, each lane is a sequential float32 chain over its blocks, and
+// the 8 lanes meet in one adjacent-pair tree. So a CTA of 8 warps maps
+//     warp w      <->  lane w (block position w inside every 144-byte chunk)
+//     thread i    <->  row i of a 32-row group
+// and every thread runs one lane chain of one row on its own: no shuffles,
+// no order bookkeeping. The tree is done once per row group through shared
+// memory, in tree_sum's order.
+//
+// Data path:
+//   * Weights stay in the GGUF layout (rows of 18-byte blocks; 8 blocks make a
+//     16-byte-aligned 144-byte chunk). A tiled TMA tensor map views them as
+//     [chunk][row][byte of chunk]; one cp.async.bulk.tensor per stage (issued
+//     by one thread, no multicast) lands 32 rows x C chunks in shared memory
+//     as [C][32][144], completing on an mbarrier of an S-deep ring. Rows past
+//     the end come back zero-filled.
+//   * In that layout the 32 rows of a chunk sit 144 bytes apart, so the 32
+//     threads of a warp reading one block offset hit 8 distinct 16-byte bank
+//     groups per quarter warp: every weight read is a conflict-free 128-bit
+//     load. Block w of a chunk lies in the 16-byte words at 16w and 16w+16,
+//     and because w is the warp index the extraction shifts are compile-time
+//     constants (the body is instantiated per lane).
+//   * x (Q8_0) is identical for all rows: staged once per CTA in shared
+//     memory (quantised there from float32 when the caller passes float32),
+//     then held in registers when K <= 2048 (8 blocks per lane), else read by
+//     warp-wide broadcast. The block dot is 8 __dp4a: sum(n * x) - 8 * sum(x).
+//   * t = (f32(sumi) * f32(dw)) * f32(dx) as two rounded multiplies, then
+//     lane = lane + t: __fmul_rn / __fadd_rn keep nvcc from fusing them.
+#include <cuda.h>
 #include <cuda_fp16.h>
 
 #include <cstdio>
 
-#include "ptx.cuh"
-#include "q4gemv.h"
+#include "common.cuh"
 
 namespace b200 {
 
@@ -37,280 +43,175 @@ __device__ unsigned g_status;
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
+constexpr int kWarps = kThreads / 32;  // one warp per lane: kWarps == kLanes
+constexpr int kGroupRows = 32;         // rows per group: one per thread of a warp
+constexpr int kChunkRowsBytes = kGroupRows * kChunkBytes;  // one chunk of a row group: 4608 B
 constexpr int kMaxStages = 8;
-constexpr int kBarBytes = 64;  // kMaxStages mbarriers
-constexpr uint64_t kStageTimeoutNs = 2000000000ull;  // 2 s: a healthy stage lands in microseconds
-constexpr unsigned kFull = 0xffffffffu;
+constexpr int kBarBytes = 64;                           // kMaxStages mbarriers
+constexpr int kRedBytes = 2 * kWarps * kGroupRows * 4;  // double-buffered lane sums
+constexpr int kSmemAlign = 128;                         // TMA destination alignment
 
-struct GemvParams {
-    const uint8_t *region[4];
+static_assert(kWarps == kLanes, "one warp per contract lane");
+
+struct alignas(64) GemvParams {
+    CUtensorMap tmap[4];    // one per region
     float *y;
     const void *x;
-    int units_per_region;  // rows (ROWS) or row pairs (PAIRS) per region
     int rows_per_region;
-    int unit_bytes;
-    int k, nb;
+    int units_per_region;   // rows (ROWS) or row pairs (PAIRS)
+    int k, nb, nch;         // nch = 144-byte chunks per row
+    int groups_per_region;  // 32-row groups
     int ctas_per_region;
-    int su;            // units per stage
-    int stages;        // ring depth
-    int stage_stride;  // bytes per ring slot
-    int xarea_bytes;   // shared bytes for the F32-mode quantised x
+    int cps;                // chunks per stage
+    int slices;             // stages per group = ceil(nch / cps)
+    int slot_bytes;         // cps * 4608
+    int stages;             // ring depth
+    int xarea_bytes;        // shared bytes for x
     int round_mode;
     int l2_policy;
+    unsigned *status;
 };
 
-__device__ __forceinline__ int q8_round(float s, int mode) {
-    if (mode == kRoundRoundf) return static_cast<int>(roundf(s));
-    // q4_0.py:96: sign(s) * floor(|s| + 0.5f), the add rounded in float32.
-    const int m = static_cast<int>(floorf(__fadd_rn(fabsf(s), 0.5f)));
-    return s < 0.0f ? -m : m;
-}
-
-// One Q8_0 block held by 8 consecutive threads (4 values each). Returns this
-// thread's 4 int8 packed in a word; *d gets the float32 scale before rounding
-// to float16, *sum the block's int sum (all 8 threads get both).
-// q4_0.py:89-97: amax / 127, inv = d == 0 ? 0 : 1/d, both IEEE-rounded.
-__device__ __forceinline__ uint32_t q8_quant_group(float4 v, int mode, float *d, int *sum) {
-    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1, 8));
-    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2, 8));
-    amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 4, 8));
-    const float db = __fdiv_rn(amax, 127.0f);
-    const float inv = db == 0.0f ? 0.0f : __fdiv_rn(1.0f, db);
-    const int q0 = q8_round(__fmul_rn(v.x, inv), mode);
-    const int q1 = q8_round(__fmul_rn(v.y, inv), mode);
-    const int q2 = q8_round(__fmul_rn(v.z, inv), mode);
-    const int q3 = q8_round(__fmul_rn(v.w, inv), mode);
-    int s = q0 + q1 + q2 + q3;
-    s += __shfl_xor_sync(kFull, s, 1, 8);
-    s += __shfl_xor_sync(kFull, s, 2, 8);
-    s += __shfl_xor_sync(kFull, s, 4, 8);
-    *d = db;
-    *sum = s;
-    return (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
-           ((static_cast<uint32_t>(q2) & 0xffu) << 16) | ((static_cast<uint32_t>(q3) & 0xffu) << 24);
-}
-
-__device__ __forceinline__ uint64_t make_policy(int kind) {
-    if (kind == kL2EvictLast) return l2_policy_evict_last();
-    if (kind == kL2EvictNormal) return l2_policy_evict_normal();
-    return l2_policy_evict_first();
-}
-
-// Bounded mbarrier wait. Returns false (and flags the device status) after
-// kStageTimeoutNs without the phase completing.
-__device__ __forceinline__ bool wait_stage(uint64_t *bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
-    while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer_ns() - t0 > kStageTimeoutNs) {
-            atomicOr(&g_status, kStatusStageTimeout);
-            return false;
-        }
+// The contract's block term for the block at byte 18*L of the 144-byte chunk
+// at `chunk` (shared memory): t = (f32(sumi) * f32(dw)) * f32(dx).
+template <int L>
+__device__ __forceinline__ float block_term(const uint8_t *chunk, const XBlock &xb) {
+    const uint4 a = *reinterpret_cast<const uint4 *>(chunk + 16 * L);
+    const uint4 c = *reinterpret_cast<const uint4 *>(chunk + 16 * L + 16);
+    const uint32_t win[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+    // The block starts at byte 2L of the window: scale in bytes 2L..2L+1,
+    // nibble word j in bytes 2L+2+4j..2L+5+4j.
+    constexpr int kD = L / 2, kDShift = 16 * (L & 1);
+    constexpr int kN = (L + 1) / 2, kNShift = 16 * ((L + 1) & 1);
+    const uint32_t dbits = (win[kD] >> kDShift) & 0xffffu;
+    uint32_t n[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        if constexpr (kNShift == 0) n[j] = win[kN + j];
+        else n[j] = __funnelshift_r(win[kN + j], win[kN + j + 1], kNShift);
     }
-    return true;
+    return block_term_words(n, dbits, xb);
 }
 
-template <int LAYOUT, int XMODE, int T, int NI>
-__global__ void __launch_bounds__(kThreads, 2) q4_gemv_kernel(const __grid_constant__ GemvParams p) {
-    constexpr int P = 32 / T;  // rows a warp works on at once
-    constexpr int M = LAYOUT == kLayoutPairs ? 2 : 1;
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ int s_abort;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
-    uint8_t *xarea = smem + kBarBytes;
-    uint8_t *ring = smem + kBarBytes + p.xarea_bytes;
+// Stage s of this CTA (row group g0 + s / slices, K-slice s % slices): one
+// tiled TMA load of 32 rows x cps chunks. Called by one thread.
+template <int LAYOUT>
+__device__ __forceinline__ void issue_stage(const GemvParams &p, uint64_t *bars, uint8_t *ring, int region, int g0,
+                                            int s, uint64_t policy) {
+    const int g = g0 + s / p.slices, c0 = (s % p.slices) * p.cps;
+    const int slot = s % p.stages;
+    mbar_arrive_expect_tx(&bars[slot], static_cast<uint32_t>(p.slot_bytes));
+    if constexpr (LAYOUT == kLayoutPairs)
+        tma_load_4d(ring + slot * p.slot_bytes, &p.tmap[region], 0, 0, g * (kGroupRows / 2), c0, &bars[slot], policy);
+    else
+        tma_load_3d(ring + slot * p.slot_bytes, &p.tmap[region], 0, g * kGroupRows, c0, &bars[slot], policy);
+}
 
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int t = lane % T;  // thread within its row team
-    const int region = blockIdx.x / p.ctas_per_region;
-    const int cr = blockIdx.x - region * p.ctas_per_region;
-    const int u0 = static_cast<int>(static_cast<long long>(p.units_per_region) * cr / p.ctas_per_region);
-    const int u1 = static_cast<int>(static_cast<long long>(p.units_per_region) * (cr + 1) / p.ctas_per_region);
-    const int nunits = u1 - u0;
-    const int nst = (nunits + p.su - 1) / p.su;
-    const uint8_t *src = p.region[region] + static_cast<size_t>(u0) * p.unit_bytes;
+// Everything after set-up, for the warp that owns lane L. A stage is p.cps
+// chunks of a 32-row group; x is read from shared memory by broadcast. The
+// chunk loop is deliberately not unrolled: eight lane-specialised bodies have
+// to fit the instruction cache together.
+template <int LAYOUT, int L>
+__device__ __forceinline__ void gemv_body(const GemvParams &p, uint64_t *bars, float *red, const uint8_t *xs,
+                                          uint8_t *ring, int region, int g0, int g1, uint64_t policy,
+                                          int *s_abort) {
+    constexpr int M = LAYOUT == kLayoutPairs ? 2 : 1;  // rows per unit
+    constexpr int UPG = kGroupRows / M;                // units per group
+    const int lane = threadIdx.x & 31;
     const int S = p.stages;
+    const int nst = (g1 - g0) * p.slices;
 
-    if (tid == 0) {
-        s_abort = 0;
-        for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
-        fence_mbar_init();
-    }
-    __syncthreads();
-
-    // Weights do not depend on the previous kernel: start streaming them
-    // before waiting on it (programmatic dependent launch).
-    uint64_t policy = 0;
-    if (tid == 0) {
-        policy = make_policy(p.l2_policy);
-        const int first = nst < S ? nst : S;
-        for (int s = 0; s < first; ++s) {
-            const int cnt = min(p.su, nunits - s * p.su);
-            const uint32_t bytes = static_cast<uint32_t>(cnt * p.unit_bytes);
-            mbar_arrive_expect_tx(&bars[s], bytes);
-            bulk_g2s(ring + s * p.stage_stride, src + static_cast<size_t>(s) * p.su * p.unit_bytes, bytes, &bars[s],
-                     policy);
-        }
-    }
-    // Every CTA of this grid is resident once it gets here, so the next
-    // kernel in the stream may start its own weight streaming now.
-    pdl_launch_dependents();
-    pdl_wait_prior_grid();
-
-    // ---- x into registers
-    uint32_t xw[NI][8];
-    float xdv[NI];
-    int xs[NI];
-    if constexpr (XMODE == kXF32) {
-        const float *xf = static_cast<const float *>(p.x);
-        uint32_t *sq = reinterpret_cast<uint32_t *>(xarea);
-        float *sd = reinterpret_cast<float *>(xarea + p.k);
-        int *ss = reinterpret_cast<int *>(xarea + p.k + 4 * p.nb);
-        for (int b0 = 0; b0 < p.nb; b0 += kThreads / 8) {
-            const int b = b0 + tid / 8, sub = tid % 8;
-            const bool ok = b < p.nb;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (ok) v = __ldg(reinterpret_cast<const float4 *>(xf + 32 * b) + sub);
-            float d;
-            int sum;
-            const uint32_t packed = q8_quant_group(v, p.round_mode, &d, &sum);
-            if (ok) {
-                sq[8 * b + sub] = packed;
-                if (sub == 0) {
-                    sd[b] = __half2float(__float2half_rn(d));
-                    ss[b] = sum;
-                }
-            }
-        }
-        __syncthreads();
-#pragma unroll
-        for (int i = 0; i < NI; ++i) {
-            const int b = t + T * i;
-            if (b < p.nb) {
-                const uint4 a = reinterpret_cast<const uint4 *>(sq + 8 * b)[0];
-                const uint4 c = reinterpret_cast<const uint4 *>(sq + 8 * b)[1];
-                xw[i][0] = a.x; xw[i][1] = a.y; xw[i][2] = a.z; xw[i][3] = a.w;
-                xw[i][4] = c.x; xw[i][5] = c.y; xw[i][6] = c.z; xw[i][7] = c.w;
-                xdv[i] = sd[b];
-                xs[i] = ss[b];
-            } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) xw[i][j] = 0;
-                xdv[i] = 0.0f;
-                xs[i] = 0;
-            }
-        }
-    } else {
-        const uint8_t *xq = static_cast<const uint8_t *>(p.x);
-        const float *xd = reinterpret_cast<const float *>(xq + p.k);
-#pragma unroll
-        for (int i = 0; i < NI; ++i) {
-            const int b = t + T * i;
-            if (b < p.nb) {
-                const uint4 a = __ldg(reinterpret_cast<const uint4 *>(xq + 32 * b));
-                const uint4 c = __ldg(reinterpret_cast<const uint4 *>(xq + 32 * b) + 1);
-                xw[i][0] = a.x; xw[i][1] = a.y; xw[i][2] = a.z; xw[i][3] = a.w;
-                xw[i][4] = c.x; xw[i][5] = c.y; xw[i][6] = c.z; xw[i][7] = c.w;
-                xdv[i] = __ldg(xd + b);
-                int s = 0;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) s = __dp4a(static_cast<int>(xw[i][j]), 0x01010101, s);
-                xs[i] = s;
-            } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) xw[i][j] = 0;
-                xdv[i] = 0.0f;
-                xs[i] = 0;
-            }
-        }
-    }
-
-    // ---- stream the stages
-    const int odd = t & 1;  // block b = t + T*i has b & 1 == t & 1 (T even)
-    const uint32_t nib_shift = odd ? 32u : 16u;
-    const uint32_t d_shift = odd ? 16u : 0u;
+    float acc = 0.0f;
     int s = 0;
     for (; s < nst; ++s) {
         const int slot = s % S;
-        const bool landed = wait_stage(&bars[slot], static_cast<uint32_t>((s / S) & 1));
-        if (!landed) s_abort = 1;
-        const uint8_t *sbuf = ring + slot * p.stage_stride;
-        const int cnt = min(p.su, nunits - s * p.su);
-        const int rows_here = cnt * M;
-        for (int base = warp * P; base < rows_here; base += kWarps * P) {
-            const int rl = base + lane / T;
-            const bool vrow = landed && rl < rows_here;
-            const int ul = M == 2 ? (rl >> 1) : rl;
-            const int mem = M == 2 ? (rl & 1) : 0;
-            const uint8_t *ub = sbuf + ul * p.unit_bytes;
-            float acc = 0.0f;
-#pragma unroll
-            for (int i = 0; i < NI; ++i) {
-                const int b = t + T * i;
-                float v = 0.0f;
-                if (vrow && b < p.nb) {
-                    const int off = LAYOUT == kLayoutPairs ? (2 * (b >> 3) + mem) * kChunkBytes + kBlockBytes * (b & 7)
-                                                           : kBlockBytes * b;
-                    const uint32_t *wp = reinterpret_cast<const uint32_t *>(ub + off - 2 * odd);
-                    const uint32_t w0 = wp[0], w1 = wp[1], w2 = wp[2], w3 = wp[3], w4 = wp[4];
-                    const uint32_t n0 = __funnelshift_rc(w0, w1, nib_shift);
-                    const uint32_t n1 = __funnelshift_rc(w1, w2, nib_shift);
-                    const uint32_t n2 = __funnelshift_rc(w2, w3, nib_shift);
-                    const uint32_t n3 = __funnelshift_rc(w3, w4, nib_shift);
-                    const uint32_t dbits = __funnelshift_rc(w0, w1, d_shift) & 0xffffu;
-                    int sumi = -8 * xs[i];
-                    sumi = __dp4a(static_cast<int>(n0 & 0x0f0f0f0fu), static_cast<int>(xw[i][0]), sumi);
-                    sumi = __dp4a(static_cast<int>(n1 & 0x0f0f0f0fu), static_cast<int>(xw[i][1]), sumi);
-                    sumi = __dp4a(static_cast<int>(n2 & 0x0f0f0f0fu), static_cast<int>(xw[i][2]), sumi);
-                    sumi = __dp4a(static_cast<int>(n3 & 0x0f0f0f0fu), static_cast<int>(xw[i][3]), sumi);
-                    sumi = __dp4a(static_cast<int>((n0 >> 4) & 0x0f0f0f0fu), static_cast<int>(xw[i][4]), sumi);
-                    sumi = __dp4a(static_cast<int>((n1 >> 4) & 0x0f0f0f0fu), static_cast<int>(xw[i][5]), sumi);
-                    sumi = __dp4a(static_cast<int>((n2 >> 4) & 0x0f0f0f0fu), static_cast<int>(xw[i][6]), sumi);
-                    sumi = __dp4a(static_cast<int>((n3 >> 4) & 0x0f0f0f0fu), static_cast<int>(xw[i][7]), sumi);
-                    const float dw = __half2float(__ushort_as_half(static_cast<unsigned short>(dbits)));
-                    v = __fmul_rn(__fmul_rn(__int2float_rn(sumi), dw), xdv[i]);
-                }
-                // Lane (t mod 8) receives blocks t, t+8, t+16, t+24 of this
-                // step, in that order: add them sequentially.
-                if constexpr (T == 32) {
-                    const float v1 = __shfl_down_sync(kFull, v, 8);
-                    const float v2 = __shfl_down_sync(kFull, v, 16);
-                    const float v3 = __shfl_down_sync(kFull, v, 24);
-                    acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, v), v1), v2), v3);
-                } else if constexpr (T == 16) {
-                    const float v1 = __shfl_down_sync(kFull, v, 8, 16);
-                    acc = __fadd_rn(__fadd_rn(acc, v), v1);
-                } else {
-                    acc = __fadd_rn(acc, v);
-                }
-            }
-            // tree_sum over the 8 lanes held by threads t = 0..7.
-            acc = __fadd_rn(acc, __shfl_xor_sync(kFull, acc, 1, 8));
-            acc = __fadd_rn(acc, __shfl_xor_sync(kFull, acc, 2, 8));
-            acc = __fadd_rn(acc, __shfl_xor_sync(kFull, acc, 4, 8));
-            if (vrow && t == 0) {
-                const int u = u0 + s * p.su + ul;
-                const int row = region * p.rows_per_region + (M == 2 ? u + mem * p.units_per_region : u);
-                p.y[row] = acc;
-            }
+        const int gi = s / p.slices, sl = s % p.slices;
+        if (!wait_stage(&bars[slot], static_cast<uint32_t>((s / S) & 1), p.status)) *s_abort = 1;
+        const uint8_t *rowbase = ring + slot * p.slot_bytes + lane * kChunkBytes;
+        const int c0 = sl * p.cps, cc = min(p.cps, p.nch - c0);
+#pragma unroll 1
+        for (int j = 0; j < cc; ++j) {
+            XBlock xb;
+            load_xblock_smem(xs, p.k, 8 * (c0 + j) + L, xb);
+            acc = __fadd_rn(acc, block_term<L>(rowbase + j * kChunkRowsBytes, xb));
+        }
+        const bool last_slice = sl == p.slices - 1;
+        float *rbuf = red + (gi & 1) * (kWarps * kGroupRows);
+        if (last_slice) {
+            rbuf[L * kGroupRows + lane] = acc;
+            acc = 0.0f;
         }
         __syncthreads();
-        if (s_abort) break;
-        if (tid == 0 && s + S < nst) {
-            const int cnt2 = min(p.su, nunits - (s + S) * p.su);
-            const uint32_t bytes = static_cast<uint32_t>(cnt2 * p.unit_bytes);
-            mbar_arrive_expect_tx(&bars[slot], bytes);
-            bulk_g2s(ring + slot * p.stage_stride, src + static_cast<size_t>(s + S) * p.su * p.unit_bytes, bytes,
-                     &bars[slot], policy);
+        if (*s_abort) break;
+        if (L == 0 && lane == 0 && s + S < nst) issue_stage<LAYOUT>(p, bars, ring, region, g0, s + S, policy);
+        if (L == 1 && last_slice) {
+            // tree_sum over the 8 lanes (q4_0.py:67-78): ((0+1)+(2+3))+((4+5)+(6+7)).
+            const float *r = rbuf + lane;
+            const float yv = tree8(r[0 * kGroupRows], r[1 * kGroupRows], r[2 * kGroupRows], r[3 * kGroupRows],
+                                   r[4 * kGroupRows], r[5 * kGroupRows], r[6 * kGroupRows], r[7 * kGroupRows]);
+            // group row `lane` is unit lane / M, member lane % M; a pair is rows
+            // u and u + units_per_region (gemv2_dev.h:46-49)
+            const int u = (g0 + gi) * UPG + (M == 2 ? lane >> 1 : lane);
+            if (u < p.units_per_region)
+                p.y[region * p.rows_per_region + u + (M == 2 ? (lane & 1) * p.units_per_region : 0)] = yv;
         }
     }
-    if (s < nst && tid == 0) {
-        // Aborted on a stage timeout: let copies already in flight land
-        // (each wait bounded) before the CTA's shared memory goes away.
+    if (s < nst && L == 0 && lane == 0) {
+        // Aborted on a stage timeout: let copies already in flight land (each
+        // wait bounded) before the CTA's shared memory goes away.
         const int issued = min(nst, s + S);
-        for (int r = s; r < issued; ++r) (void)wait_stage(&bars[r % S], static_cast<uint32_t>((r / S) & 1));
+        for (int r = s; r < issued; ++r) (void)wait_stage(&bars[r % S], static_cast<uint32_t>((r / S) & 1), p.status);
+    }
+}
+
+template <int LAYOUT, int XMODE>
+__global__ void __launch_bounds__(kThreads, 1) q4_gemv_kernel(const __grid_constant__ GemvParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ int s_abort;
+    uint8_t *ring = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + kSmemAlign - 1) & ~static_cast<uintptr_t>(kSmemAlign - 1));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + p.stages * p.slot_bytes);
+    float *red = reinterpret_cast<float *>(ring + p.stages * p.slot_bytes + kBarBytes);
+    uint8_t *xs = ring + p.stages * p.slot_bytes + kBarBytes + kRedBytes;
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int region = blockIdx.x / p.ctas_per_region;
+    const int cr = blockIdx.x - region * p.ctas_per_region;
+    const int g0 = static_cast<int>(static_cast<long long>(p.groups_per_region) * cr / p.ctas_per_region);
+    const int g1 = static_cast<int>(static_cast<long long>(p.groups_per_region) * (cr + 1) / p.ctas_per_region);
+
+    if (tid == 0) {
+        s_abort = 0;
+        prefetch_tmap(&p.tmap[region]);
+        for (int s = 0; s < p.stages; ++s) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const uint64_t policy = make_policy(p.l2_policy);
+
+    // Weights do not depend on the previous kernel: start streaming them
+    // before waiting on it. Every CTA of this grid is resident here, so the
+    // next kernel in the stream may launch now (programmatic dependent launch).
+    if (tid == 0) {
+        const int nst = (g1 - g0) * p.slices;
+        const int first = nst < p.stages ? nst : p.stages;
+        for (int s = 0; s < first; ++s) issue_stage<LAYOUT>(p, bars, ring, region, g0, s, policy);
+    }
+    pdl_launch_dependents();
+    pdl_wait_prior_grid();
+
+    stage_x<XMODE>(p.x, p.k, p.round_mode, xs);
+    __syncthreads();
+
+    switch (warp) {
+        case 0: gemv_body<LAYOUT, 0>(p, bars, red, xs, ring, region, g0, g1, policy, &s_abort); break;
+        case 1: gemv_body<LAYOUT, 1>(p, bars, red, xs, ring, region, g0, g1, policy, &s_abort); break;
+        case 2: gemv_body<LAYOUT, 2>(p, bars, red, xs, ring, region, g0, g1, policy, &s_abort); break;
+        case 3: gemv_body<LAYOUT, 3>(p, bars, red, xs, ring, region, g0, g1, policy, &s_abort); break;
+        case 4: gemv_body<LAYOUT, 4>(p, bars, red, xs, ring, region, g0, g1, policy, &s_abort); break;
+        case 5: gemv_body<LAYOUT, 5>(p, bars, red, xs, ring, region, g0, g1, policy, &s_abort); break;
+        case 6: gemv_body<LAYOUT, 6>(p, bars, red, xs, ring, region, g0, g1, policy, &s_abort); break;
+        default: gemv_body<LAYOUT, 7>(p, bars, red, xs, ring, region, g0, g1, policy, &s_abort); break;
     }
 }
 
@@ -352,43 +253,23 @@ __global__ void l2_prefetch_kernel(const uint8_t *r0, const uint8_t *r1, const u
 
 using KernelFn = void (*)(GemvParams);
 
-template <int LAYOUT, int XMODE>
-KernelFn pick(int T, int NI) {
-    if (T == 32) {
-        switch (NI) {
-            case 1: return q4_gemv_kernel<LAYOUT, XMODE, 32, 1>;
-            case 2: return q4_gemv_kernel<LAYOUT, XMODE, 32, 2>;
-            case 3: return q4_gemv_kernel<LAYOUT, XMODE, 32, 3>;
-            case 4: return q4_gemv_kernel<LAYOUT, XMODE, 32, 4>;
-            case 5: return q4_gemv_kernel<LAYOUT, XMODE, 32, 5>;
-            case 6: return q4_gemv_kernel<LAYOUT, XMODE, 32, 6>;
-            case 7: return q4_gemv_kernel<LAYOUT, XMODE, 32, 7>;
-            case 8: return q4_gemv_kernel<LAYOUT, XMODE, 32, 8>;
-        }
-    } else if (T == 16) {
-        if (NI == 1) return q4_gemv_kernel<LAYOUT, XMODE, 16, 1>;
-        if (NI == 2) return q4_gemv_kernel<LAYOUT, XMODE, 16, 2>;
-    } else if (T == 8) {
-        if (NI == 1) return q4_gemv_kernel<LAYOUT, XMODE, 8, 1>;
-        if (NI == 2) return q4_gemv_kernel<LAYOUT, XMODE, 8, 2>;
-    }
-    return nullptr;
+KernelFn pick_kernel(int layout, int xmode) {
+    if (layout == kLayoutRows) return xmode == kXF32 ? q4_gemv_kernel<kLayoutRows, kXF32> : q4_gemv_kernel<kLayoutRows, kXPacked>;
+    return xmode == kXF32 ? q4_gemv_kernel<kLayoutPairs, kXF32> : q4_gemv_kernel<kLayoutPairs, kXPacked>;
 }
 
-KernelFn pick_kernel(int layout, int xmode, int T, int NI) {
-    if (layout == kLayoutRows) return xmode == kXF32 ? pick<kLayoutRows, kXF32>(T, NI) : pick<kLayoutRows, kXPacked>(T, NI);
-    return xmode == kXF32 ? pick<kLayoutPairs, kXF32>(T, NI) : pick<kLayoutPairs, kXPacked>(T, NI);
-}
+}  // namespace
 
 constexpr int kMaxDevices = 64;
 
 struct DeviceInfo {
     int sms = 0;
     int smem_optin = 0;
+    unsigned *status = nullptr;
 };
 
 // Per-device attributes, read once (launch paths are latency-critical).
-const DeviceInfo *device_info() {
+static DeviceInfo *device_info() {
     static DeviceInfo info[kMaxDevices];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
@@ -397,6 +278,9 @@ const DeviceInfo *device_info() {
         int sms = 0, smem = 0;
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return nullptr;
         if (cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return nullptr;
+        void *st = nullptr;
+        if (cudaGetSymbolAddress(&st, g_status) != cudaSuccess) return nullptr;
+        d.status = static_cast<unsigned *>(st);
         d.smem_optin = smem;
         d.sms = sms;
     }
@@ -413,9 +297,13 @@ int max_smem_optin() {
     return d ? d->smem_optin : 0;
 }
 
-// Raise a kernel's dynamic shared-memory limit once per (kernel, device).
-bool ensure_smem(KernelFn fn, int bytes) {
-    struct Entry { KernelFn fn; int dev; int bytes; };
+unsigned *status_word() {
+    const DeviceInfo *d = device_info();
+    return d ? d->status : nullptr;
+}
+
+bool ensure_smem(const void *fn, int bytes) {
+    struct Entry { const void *fn; int dev; int bytes; };
     static Entry cache[256];
     static int used = 0;
     int dev = 0;
@@ -427,7 +315,24 @@ bool ensure_smem(KernelFn fn, int bytes) {
     return true;
 }
 
-inline int round_up(int v, int a) { return (v + a - 1) / a * a; }
+int resident_ctas(const void *fn, int threads, int smem) {
+    struct Entry { const void *fn; int dev; int threads; int smem; int ctas; };
+    static Entry cache[512];
+    static int used = 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 1;
+    for (int i = 0; i < used; ++i)
+        if (cache[i].fn == fn && cache[i].dev == dev && cache[i].threads == threads && cache[i].smem == smem)
+            return cache[i].ctas;
+    if (!ensure_smem(fn, smem)) return 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, static_cast<size_t>(smem)) != cudaSuccess || n < 1)
+        n = 1;
+    if (used < 512) cache[used++] = Entry{fn, dev, threads, smem, n};
+    return n;
+}
+
+namespace {
 
 struct Plan {
     GemvParams p;
@@ -436,50 +341,101 @@ struct Plan {
     int smem;
 };
 
-int make_plan(const GemvLaunch &L, const Tuning &tu, Plan *out) {
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    }
+    return fn;
+}
+
+// The weight view the kernel streams: [chunk][row][byte of chunk] (ROWS), or
+// [chunk][pair][member][byte of chunk] (PAIRS), box = 32 rows x cps chunks,
+// landing in shared memory as [cps][32][144].
+int encode_region(CUtensorMap *map, int layout, const uint8_t *base, int rows, int k, int cps) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return kErrCuda;
+    const cuuint64_t nch = static_cast<cuuint64_t>(k / 256);
+    const cuuint64_t row_bytes = static_cast<cuuint64_t>(k / kQK) * kBlockBytes;
+    CUresult r;
+    if (layout == kLayoutPairs) {
+        const cuuint64_t dims[4] = {kChunkBytes, 2, static_cast<cuuint64_t>(rows / 2), nch};
+        const cuuint64_t strides[3] = {kChunkBytes, 2 * row_bytes, 2 * kChunkBytes};
+        const cuuint32_t box[4] = {kChunkBytes, 2, kGroupRows / 2, static_cast<cuuint32_t>(cps)};
+        const cuuint32_t estr[4] = {1, 1, 1, 1};
+        r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t *>(base), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        const cuuint64_t dims[3] = {kChunkBytes, static_cast<cuuint64_t>(rows), nch};
+        const cuuint64_t strides[2] = {row_bytes, kChunkBytes};
+        const cuuint32_t box[3] = {kChunkBytes, kGroupRows, static_cast<cuuint32_t>(cps)};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t *>(base), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    return r == CUDA_SUCCESS ? 0 : kErrInval;
+}
+
+int make_plan(const GemvLaunch &L, const Tuning &tu, bool encode, Plan *out) {
     const char *why = nullptr;
     if (int rc = gemv_validate(L, &why)) return rc;
-    const int nb = L.k / kQK, row_bytes = nb * kBlockBytes;
+    const int nb = L.k / kQK, nch = nb / kLanes;
     const int M = L.layout == kLayoutPairs ? 2 : 1;
-    const int T = nb >= 32 ? 32 : (nb >= 16 ? 16 : 8);
-    const int NI = (nb + T - 1) / T;
-    KernelFn fn = pick_kernel(L.layout, L.xmode, T, NI);
+    KernelFn fn = pick_kernel(L.layout, L.xmode);
     if (!fn) return kErrInval;
     GemvParams p{};
-    for (int r = 0; r < 4; ++r) p.region[r] = L.region[r < L.nregions ? r : 0];
+    p.status = status_word();
+    if (!p.status) return kErrNoDev;
     p.y = L.y;
     p.x = L.x;
     p.rows_per_region = L.rows / L.nregions;
     p.units_per_region = p.rows_per_region / M;
-    p.unit_bytes = M * row_bytes;
     p.k = L.k;
     p.nb = nb;
+    p.nch = nch;
     p.round_mode = L.round_mode;
     p.l2_policy = L.l2_policy;
+    p.groups_per_region = (p.rows_per_region + kGroupRows - 1) / kGroupRows;
+    p.xarea_bytes = round_up(L.k + 8 * nb, 16);
+    int cps = tu.stage_bytes / kChunkRowsBytes;
+    if (cps < 1) cps = 1;
+    if (cps > nch) cps = nch;
+    p.cps = cps;
+    p.slices = (nch + cps - 1) / cps;
+    p.slot_bytes = cps * kChunkRowsBytes;
     p.stages = tu.stages < 1 ? 1 : (tu.stages > kMaxStages ? kMaxStages : tu.stages);
-    int su = tu.stage_bytes / p.unit_bytes;
-    if (su < 1) su = 1;
-    if (su > p.units_per_region) su = p.units_per_region;
-    p.xarea_bytes = L.xmode == kXF32 ? round_up(L.k + 8 * nb, 128) : 0;
     const int limit = max_smem_optin();
-    for (;;) {
-        p.su = su;
-        p.stage_stride = round_up(su * p.unit_bytes + 16, 128);
-        const int smem = kBarBytes + p.xarea_bytes + p.stages * p.stage_stride;
-        if (smem <= limit || (su == 1 && p.stages == 1)) break;
-        if (su > 1) su = (su + 1) / 2;
-        else p.stages -= 1;
-    }
-    const int smem = kBarBytes + p.xarea_bytes + p.stages * p.stage_stride;
+    const int fixed = kSmemAlign + kBarBytes + kRedBytes + p.xarea_bytes;
+    while (p.stages > 1 && fixed + p.stages * p.slot_bytes > limit) p.stages -= 1;
+    const int smem = fixed + p.stages * p.slot_bytes;
     if (smem > limit) return kErrInval;
     const int sms = sm_count();
     if (sms <= 0) return kErrNoDev;
-    const int target = sms * (tu.ctas_per_sm < 1 ? 1 : tu.ctas_per_sm);
-    const int stages_per_region = (p.units_per_region + su - 1) / su;
+    int per_sm = tu.ctas_per_sm < 1 ? 1 : tu.ctas_per_sm;
+    const int fit = resident_ctas(reinterpret_cast<const void *>(fn), kThreads, smem);
+    if (per_sm > fit) per_sm = fit;  // one wave: every CTA resident at once
+    const int target = sms * per_sm;
     int cpr = target / L.nregions;
     if (cpr < 1) cpr = 1;
-    if (cpr > stages_per_region) cpr = stages_per_region;
+    if (cpr > p.groups_per_region) cpr = p.groups_per_region;
     p.ctas_per_region = cpr;
+    if (encode) {
+        for (int r = 0; r < L.nregions; ++r)
+            if (int rc = encode_region(&p.tmap[r], L.layout, L.region[r], p.rows_per_region, L.k, cps)) return rc;
+    }
     out->p = p;
     out->fn = fn;
     out->grid = cpr * L.nregions;
@@ -511,7 +467,7 @@ int gemv_validate(const GemvLaunch &L, const char **why) {
 
 int gemv_grid(const GemvLaunch &L, const Tuning &tu, int *grid, int *smem_bytes) {
     Plan pl;
-    if (int rc = make_plan(L, tu, &pl)) return rc;
+    if (int rc = make_plan(L, tu, false, &pl)) return rc;
     if (grid) *grid = pl.grid;
     if (smem_bytes) *smem_bytes = pl.smem;
     return 0;
@@ -519,8 +475,8 @@ int gemv_grid(const GemvLaunch &L, const Tuning &tu, int *grid, int *smem_bytes)
 
 int gemv_launch(const GemvLaunch &L, const Tuning &tu, cudaStream_t stream) {
     Plan pl;
-    if (int rc = make_plan(L, tu, &pl)) return rc;
-    if (!ensure_smem(pl.fn, pl.smem)) return kErrCuda;
+    if (int rc = make_plan(L, tu, true, &pl)) return rc;
+    if (!ensure_smem(reinterpret_cast<const void *>(pl.fn), pl.smem)) return kErrCuda;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(pl.grid);
     cfg.blockDim = dim3(kThreads);

@@ -54,6 +54,7 @@ struct Tuning {
     int stage_bytes = 16384;  // target bytes per pipeline stage
     int stages = 4;           // stages in flight per CTA
     int ctas_per_sm = 2;      // grid = SMs x this, at most one CTA per stage
+    int xreg_chunks = 8;      // rows of at most this many 144-byte chunks keep x in registers
 };
 
 // Error codes shared with the C ABI (negative errno values).
@@ -73,6 +74,40 @@ int quantize_launch(const float *x, uint8_t *xpacked, int k, int round_mode, cud
 
 // Pull `bytes` bytes at each region start into L2 (gemv2's fetch-ahead).
 int prefetch_l2_launch(const uint8_t *const *region, int nregions, size_t bytes_per_region, cudaStream_t stream);
+
+// ----------------------------------------------------------- tile layout
+// The engine's re-laid weights (see q4tile.cu): rows padded to a multiple of
+// kTileRows; tile (group g, chunk c) of kTileBytes at ((g * k/256) + c) * kTileBytes.
+constexpr int kTileRows = 16;
+constexpr int kTileBytes = kTileRows * kLanes * kBlockBytes;  // 2304
+
+struct TileLaunch {
+    const uint8_t *w = nullptr;  // tiles
+    int rows = 0;
+    int k = 0;
+    int xmode = kXPacked;
+    const void *x = nullptr;
+    float *y = nullptr;
+    int round_mode = kRoundContract;
+    int l2_policy = kL2EvictFirst;
+    bool pdl = false;
+};
+
+size_t tiled_bytes(int rows, int k);  // 0 for an unusable shape
+int tile_validate(const TileLaunch &L, const char **why);
+int tile_launch(const TileLaunch &L, const Tuning &tu, cudaStream_t stream);
+int tile_grid(const TileLaunch &L, const Tuning &tu, int *grid, int *smem_bytes);
+// GGUF Q4_0 rows (2-byte aligned) -> tiles (16-byte aligned, tiled_bytes(rows, k) bytes).
+int repack_launch(const uint8_t *src_rows, int rows, int k, uint8_t *dst_tiles, cudaStream_t stream);
+
+// ----------------------------------------------------------- greedy pick
+// First index of the largest of y[0..n) (tp_llama.cpp:879-882), plus
+// index_base, into *out_index / *out_value. `scratch` holds
+// argmax_scratch_bytes() bytes of per-CTA candidates.
+constexpr int kArgmaxMaxParts = 1024;
+int argmax_scratch_bytes();
+int argmax_launch(const float *y, int n, int index_base, void *scratch, int *out_index, float *out_value,
+                  cudaStream_t stream, bool pdl);
 
 int read_status(unsigned *status);   // device status word of the current device
 int clear_status();

@@ -14,6 +14,8 @@ from .capi import check, lib
 
 QK = 32
 BLOCK_BYTES = 18
+LAYOUT_ROWS = 0    # GGUF rows (B200_LAYOUT_ROWS)
+LAYOUT_TILES = 1   # the engine's re-laid tiles (B200_LAYOUT_TILES)
 
 
 def _torch():
@@ -37,18 +39,23 @@ def current_stream_handle(device: int) -> int:
     return int(torch.cuda.current_stream(device).cuda_stream)
 
 
-class QMat:
-    """A Q4_0 matrix in device memory, GGUF row layout (b200_qmat_t)."""
+def tiled_bytes(rows: int, k: int) -> int:
+    return int(lib().b200_tiled_bytes(rows, k))
 
-    def __init__(self, blocks, rows: int, k: int):
+
+class QMat:
+    """A Q4_0 matrix in device memory (b200_qmat_t): GGUF rows, or the
+    engine's tiles (Engine.repack)."""
+
+    def __init__(self, blocks, rows: int, k: int, layout: int = LAYOUT_ROWS):
         if k % QK:
             raise ValueError(f"in_features must be a multiple of {QK}, got {k}")
-        nbytes = rows * (k // QK) * BLOCK_BYTES
+        nbytes = rows * (k // QK) * BLOCK_BYTES if layout == LAYOUT_ROWS else tiled_bytes(rows, k)
         if hasattr(blocks, "numel") and blocks.numel() * blocks.element_size() < nbytes:
-            raise ValueError("blocks tensor is smaller than rows * k/32 * 18 bytes")
+            raise ValueError(f"blocks tensor is smaller than the {nbytes} bytes of a {rows}x{k} matrix")
         self.blocks = blocks          # keeps the allocation alive
-        self.rows, self.k = rows, k
-        self.c = capi.b200_qmat_t(dev_ptr(blocks), rows, k)
+        self.rows, self.k, self.layout = rows, k, layout
+        self.c = capi.b200_qmat_t(dev_ptr(blocks), rows, k, layout)
 
     @classmethod
     def from_numpy(cls, blocks_np, device: int = 0) -> "QMat":
@@ -59,6 +66,7 @@ class QMat:
 
     @property
     def nbytes(self) -> int:
+        """Algorithmic weight bytes (18 per 32 weights), whatever the layout."""
         return self.rows * (self.k // QK) * BLOCK_BYTES
 
 
@@ -115,6 +123,33 @@ class Engine:
     def quantize(self, x, xpacked, k: int) -> None:
         check(lib().b200_quantize_q8_0(self.h, dev_ptr(x), dev_ptr(xpacked), k), "b200_quantize_q8_0")
 
+    def repack(self, W: QMat) -> QMat:
+        """GGUF rows -> a new tiled matrix on this engine's device (b200_repack_q4_0)."""
+        torch = _torch()
+        if W.layout != LAYOUT_ROWS:
+            raise ValueError("repack takes a GGUF-row matrix")
+        n = tiled_bytes(W.rows, W.k)
+        if n == 0:
+            raise ValueError(f"cannot tile a {W.rows}x{W.k} matrix")
+        dst = torch.empty(n, dtype=torch.uint8, device=f"cuda:{self.device}")
+        check(lib().b200_repack_q4_0(self.h, W.c.w, W.rows, W.k, dev_ptr(dst)), "b200_repack_q4_0")
+        return QMat(dst, W.rows, W.k, LAYOUT_TILES)
+
+    def argmax(self, y, n: int, out, index_base: int = 0) -> None:
+        """First index of the largest of y[:n] (+ index_base) and its value -> out (8 bytes: int32, float32)."""
+        check(lib().b200_argmax_f32(self.h, dev_ptr(y), n, index_base, dev_ptr(out)), "b200_argmax_f32")
+
+    def capture_begin(self) -> None:
+        check(lib().b200_capture_begin(self.h), "b200_capture_begin")
+
+    def capture_end(self) -> "Graph":
+        g = ctypes.c_void_p()
+        check(lib().b200_capture_end(self.h, ctypes.byref(g)), "b200_capture_end")
+        return Graph(self, g)
+
+    def copy_async(self, dst: int, src: int, nbytes: int) -> None:
+        check(lib().b200_copy_async(self.h, dst, src, nbytes), "b200_copy_async")
+
     def prefetch(self, W: QMat) -> None:
         check(lib().b200_prefetch(self.h, ctypes.byref(W.c)), "b200_prefetch")
 
@@ -126,11 +161,32 @@ class Engine:
         check(lib().b200_engine_status(self.h, ctypes.byref(s)), "b200_engine_status")
         return int(s.value)
 
-    def plan(self, rows: int, k: int, fused_f32: bool = False) -> tuple[int, int]:
+    def plan(self, rows: int, k: int, fused_f32: bool = False, layout: int = LAYOUT_TILES) -> tuple[int, int]:
         g, sm = ctypes.c_int(0), ctypes.c_int(0)
-        check(lib().b200_gemv_plan(self.h, rows, k, int(fused_f32), ctypes.byref(g), ctypes.byref(sm)),
+        check(lib().b200_gemv_plan(self.h, rows, k, layout, int(fused_f32), ctypes.byref(g), ctypes.byref(sm)),
               "b200_gemv_plan")
         return g.value, sm.value
+
+
+class Graph:
+    """A captured sequence of engine calls (b200_graph_t)."""
+
+    def __init__(self, engine: Engine, handle):
+        self.engine, self.h = engine, handle
+
+    def launch(self) -> None:
+        check(lib().b200_graph_launch(self.engine.h, self.h), "b200_graph_launch")
+
+    def close(self) -> None:
+        if self.h:
+            lib().b200_graph_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class GemvDev:

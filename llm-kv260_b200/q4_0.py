@@ -99,7 +99,7 @@ def gemv_q4_0(blocks: np.ndarray, k: int, xq: np.ndarray, xd: np.ndarray, device
 
 
 def gemv_q4_0_f32(blocks: np.ndarray, k: int, x: np.ndarray, device: int = 0) -> np.ndarray:
-    """q4_0.py:185-188 on the GPU, through the engine's fused call (b200_gemv_f32)."""
+    """q4_0.py:185-188 on the GPU, through the engine's call (b200_repack_q4_0 then b200_gemv_f32)."""
     if x.dtype != np.float32:
         raise TypeError(f"activations must be float32, got {x.dtype}")
     n = _check_blocks(blocks, k)
@@ -107,10 +107,10 @@ def gemv_q4_0_f32(blocks: np.ndarray, k: int, x: np.ndarray, device: int = 0) ->
         raise ValueError(f"x shape {x.shape} does not match K={k}")
     torch = _torch()
     from .engine import QMat
-    W = QMat(_to_dev(blocks, device), n, k)
+    e = engine(device)
+    W = e.repack(QMat(_to_dev(blocks, device), n, k))   # the engine re-lays weights at load
     x_t = _to_dev(x, device)
     y_t = torch.empty(n, dtype=torch.float32, device=f"cuda:{device}")
-    e = engine(device)
     e.gemv_f32(W, x_t, y_t)
     e.sync()
     return y_t.cpu().numpy()

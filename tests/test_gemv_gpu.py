@@ -41,9 +41,11 @@ def _dev(torch, a: np.ndarray):
     return torch.from_numpy(np.ascontiguousarray(a).reshape(-1).view(np.uint8).copy()).cuda()
 
 
-def _run_engine(torch, pkg, eng, blocks, k, x, fuse=0, packed=False, oracle=None, **cfg):
+def _run_engine(torch, pkg, eng, blocks, k, x, fuse=0, packed=False, oracle=None, layout=1, **cfg):
     n = blocks.shape[0]
     W = pkg.QMat(_dev(torch, blocks), n, k)
+    if layout == pkg.LAYOUT_TILES:
+        W = eng.repack(W)
     y = torch.full((n,), float("nan"), dtype=torch.float32, device="cuda")
     eng.configure(fuse_quantize=fuse, **cfg)
     if packed:
@@ -54,18 +56,19 @@ def _run_engine(torch, pkg, eng, blocks, k, x, fuse=0, packed=False, oracle=None
         eng.gemv_f32(W, torch.from_numpy(x).cuda(), y)
     eng.sync()
     out = y.cpu().numpy()
-    eng.configure(fuse_quantize=0, stage_bytes=16384, stages=4, ctas_per_sm=2)
+    eng.configure(fuse_quantize=0, stage_bytes=16384, stages=4, ctas_per_sm=2, xreg_chunks=8)
     return out
 
 
 # ------------------------------------------------------------ golden pins
 
+@pytest.mark.parametrize("layout", [0, 1])
 @pytest.mark.parametrize("fuse", [0, 1])
-def test_golden_vector_on_gpu(torch_mod, pkg, eng, oracle, fuse):
+def test_golden_vector_on_gpu(torch_mod, pkg, eng, oracle, fuse, layout):
     """The reference's frozen digest (tests/test_q4_0_contract.py:181-191)."""
     blocks = oracle.quantize_q4_0(cases.std_weights(96, 2048, 2024))
     x = cases.std_weights(1, 2048, 2025)[0]
-    y = _run_engine(torch_mod, pkg, eng, blocks, 2048, x, fuse=fuse)
+    y = _run_engine(torch_mod, pkg, eng, blocks, 2048, x, fuse=fuse, layout=layout)
     assert cases.sha256(y) == cases.CONTRACT_GOLDEN_SHA256
 
 
@@ -95,9 +98,12 @@ def test_llama_1b_shapes(torch_mod, pkg, eng, oracle, golden, name, n, k, seed):
     blocks = oracle.quantize_q4_0(cases.shape_weights(n, k, seed))
     assert cases.sha256(blocks) == rec["sha256_blocks"]
     x = cases.shape_x(k, seed)
-    for fuse in (0, 1):
-        assert cases.sha256(_run_engine(torch_mod, pkg, eng, blocks, k, x, fuse=fuse)) == rec["sha256_y"], fuse
-    assert cases.sha256(_run_engine(torch_mod, pkg, eng, blocks, k, x, packed=True, oracle=oracle)) == rec["sha256_y"]
+    for layout in (0, 1):
+        for fuse in (0, 1):
+            y = _run_engine(torch_mod, pkg, eng, blocks, k, x, fuse=fuse, layout=layout)
+            assert cases.sha256(y) == rec["sha256_y"], (layout, fuse)
+        y = _run_engine(torch_mod, pkg, eng, blocks, k, x, packed=True, oracle=oracle, layout=layout)
+        assert cases.sha256(y) == rec["sha256_y"], layout
 
 
 @pytest.mark.parametrize("name", sorted(cases.K_SPLIT))
@@ -109,7 +115,7 @@ def test_ksplit_shards_with_ordered_sum(torch_mod, pkg, eng, oracle, golden, nam
     x = cases.shape_x(k, seed)
     kk = k // parts
     partials = [_run_engine(torch_mod, pkg, eng, cases.k_slice_blocks(blocks, k, r, parts), kk,
-                            np.ascontiguousarray(x[r * kk:(r + 1) * kk])) for r in range(parts)]
+                            np.ascontiguousarray(x[r * kk:(r + 1) * kk]), layout=r % 2) for r in range(parts)]
     assert cases.sha256(oracle.allreduce_ordered(partials)) == golden["shapes"][name][f"sha256_ksplit{parts}"]
 
 
@@ -122,18 +128,23 @@ def test_every_team_width_and_blocks_per_thread(torch_mod, pkg, eng, oracle, k, 
     blocks = oracle.quantize_q4_0(cases.std_weights(rows, k, 1000 + k + rows))
     x = cases.std_weights(1, k, 2000 + k)[0]
     want = oracle.gemv_q4_0_f32(blocks, k, x)
-    for fuse in (0, 1):
-        got = _run_engine(torch_mod, pkg, eng, blocks, k, x, fuse=fuse)
-        assert np.array_equal(_bits(got), _bits(want)), f"k={k} rows={rows} fuse={fuse}"
+    for layout in (0, 1):
+        for fuse in (0, 1):
+            for xreg in (0, 8):
+                got = _run_engine(torch_mod, pkg, eng, blocks, k, x, fuse=fuse, layout=layout, xreg_chunks=xreg)
+                assert np.array_equal(_bits(got), _bits(want)), f"k={k} rows={rows} fuse={fuse} layout={layout}"
 
 
-@pytest.mark.parametrize("stage_bytes,stages,ctas", [(16, 1, 1), (1152, 2, 1), (4096, 3, 4), (65536, 2, 2),
-                                                     (16384, 8, 2), (200000, 1, 1)])
-def test_pipeline_shapes_do_not_change_bits(torch_mod, pkg, eng, oracle, stage_bytes, stages, ctas):
-    blocks = oracle.quantize_q4_0(cases.std_weights(1000, 2048, 31))
-    x = cases.std_weights(1, 2048, 32)[0]
-    want = oracle.gemv_q4_0_f32(blocks, 2048, x)
-    got = _run_engine(torch_mod, pkg, eng, blocks, 2048, x, stage_bytes=stage_bytes, stages=stages, ctas_per_sm=ctas)
+@pytest.mark.parametrize("layout", [0, 1])
+@pytest.mark.parametrize("k", [2048, 8192])
+@pytest.mark.parametrize("stage_bytes,stages,ctas,xreg", [(16, 1, 1, 0), (1152, 2, 1, 0), (4096, 3, 4, 8),
+                                                          (65536, 2, 2, 0), (16384, 8, 2, 8), (200000, 1, 1, 0)])
+def test_pipeline_shapes_do_not_change_bits(torch_mod, pkg, eng, oracle, stage_bytes, stages, ctas, xreg, k, layout):
+    blocks = oracle.quantize_q4_0(cases.std_weights(1000, k, 31))
+    x = cases.std_weights(1, k, 32)[0]
+    want = oracle.gemv_q4_0_f32(blocks, k, x)
+    got = _run_engine(torch_mod, pkg, eng, blocks, k, x, stage_bytes=stage_bytes, stages=stages, ctas_per_sm=ctas,
+                      xreg_chunks=xreg, layout=layout)
     assert np.array_equal(_bits(got), _bits(want))
 
 
@@ -148,9 +159,10 @@ def test_zero_and_degenerate_activations(torch_mod, pkg, eng, oracle):
     for x in (np.zeros(k, np.float32), np.full(k, -0.0, np.float32), np.tile(edge["tiny"], k // 32),
               np.tile(edge["floor_half"], k // 32), np.tile(edge["roundf_tie"], k // 32)):
         want = oracle.gemv_q4_0_f32(blocks, k, x)
-        for fuse in (0, 1):
-            got = _run_engine(torch_mod, pkg, eng, blocks, k, x, fuse=fuse)
-            assert np.array_equal(_bits(got), _bits(want))
+        for layout in (0, 1):
+            for fuse in (0, 1):
+                got = _run_engine(torch_mod, pkg, eng, blocks, k, x, fuse=fuse, layout=layout)
+                assert np.array_equal(_bits(got), _bits(want))
 
 
 # ------------------------------------------------------------ quantiser
@@ -253,6 +265,29 @@ def test_udmabuf_pool_clean_run_invalidate(torch_mod, pkg, oracle):
     dev.close()
     pool.close()
     assert np.array_equal(_bits(y), _bits(oracle.gemv_q4_0(blocks, k, xq, xd)))
+
+
+def test_repack_layout_matches_its_definition(torch_mod, pkg, eng, oracle):
+    """Tile (g, c) at ((g*nch)+c)*2304: nibbles [lane][row][16], then scales [lane][row]; padded rows zero."""
+    torch = torch_mod
+    rows, k = 37, 512
+    blocks = oracle.quantize_q4_0(cases.std_weights(rows, k, 81))
+    T = eng.repack(pkg.QMat(_dev(torch, blocks), rows, k))
+    eng.sync()
+    tiles = T.blocks.cpu().numpy()
+    nb, nch = k // 32, k // 256
+    assert tiles.size == pkg.tiled_bytes(rows, k) == 48 * nb * 18
+    for r in range(48):
+        for b in range(nb):
+            g, i, c, l = r // 16, r % 16, b // 8, b % 8
+            base = (g * nch + c) * 2304
+            nib = tiles[base + (l * 16 + i) * 16: base + (l * 16 + i) * 16 + 16]
+            sc = tiles[base + 2048 + (l * 16 + i) * 2: base + 2048 + (l * 16 + i) * 2 + 2]
+            if r < rows:
+                assert np.array_equal(nib, blocks[r, b * 18 + 2:b * 18 + 18])
+                assert np.array_equal(sc, blocks[r, b * 18:b * 18 + 2])
+            else:
+                assert not nib.any() and not sc.any()
 
 
 def test_bad_arguments_are_refused(torch_mod, pkg, oracle):
