@@ -55,7 +55,8 @@ typedef struct {
     int round_mode;      /* Q8_0 rounding: 0 floor(|s|+0.5f) as q4_0.py:96 (default), 1 roundf as tp_llama.cpp:343 */
     int fuse_quantize;   /* b200_gemv_f32: 1 quantise inside each GEMV CTA, 0 a separate quantise kernel (default 0) */
     int prefetch_next;   /* 1: a `next` hint issues an L2 prefetch of that matrix on a side stream (default 0) */
-    int xreg_chunks;     /* rows of at most this many 144-byte chunks (K <= 256*this, at most 8) keep x in registers (default 8) */
+    int xreg_chunks;     /* GGUF-row kernel: unused; kept for the layout of this struct (default 8) */
+    int kslices;         /* tile kernel: split each row's block dots over at least this many thread slices: 1, 2 or 4 (default 1) */
 } b200_engine_config_t;
 
 /* Replaces engine_t::probe + engine_t::open (tp_llama.cpp:303-317). */
@@ -85,6 +86,12 @@ B200_API uint64_t b200_tiled_bytes(int rows, int k);
 /* Re-lay GGUF Q4_0 rows at `src` (2-byte aligned) into tiles at `dst`
  * (16-byte aligned, b200_tiled_bytes(rows, k) bytes) on the engine's stream. */
 B200_API int b200_repack_q4_0(b200_engine_t *e, uint64_t src, int rows, int k, uint64_t dst);
+
+/* b200_gemv_f32 plus the greedy pick over its output, fused into the GEMV
+ * (the lm_head call of a decode token): y as b200_gemv_f32, and the 8 bytes at
+ * `out` as b200_argmax_f32 over y[0..rows). W must be in the tile layout. */
+B200_API int b200_gemv_argmax_f32(b200_engine_t *e, const b200_qmat_t *W, uint64_t x, uint64_t y, int index_base,
+                                  uint64_t out);
 
 /* Greedy pick over y[0..n) on the device, as the runtime's scan does
  * (tp_llama.cpp:879-882: first index of the largest value): writes the

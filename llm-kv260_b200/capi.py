@@ -43,7 +43,7 @@ class b200_engine_config_t(ctypes.Structure):
     """include/b200_engine.h"""
     _fields_ = [("stage_bytes", c_int), ("stages", c_int), ("ctas_per_sm", c_int), ("l2_policy", c_int),
                 ("pdl", c_int), ("round_mode", c_int), ("fuse_quantize", c_int), ("prefetch_next", c_int),
-                ("xreg_chunks", c_int)]
+                ("xreg_chunks", c_int), ("kslices", c_int)]
 
 
 P = ctypes.POINTER
@@ -91,6 +91,7 @@ SIGNATURES: dict[str, tuple] = {
     "b200_gemv_plan": (c_int, [c_vp, c_int, c_int, c_int, c_int, P(c_int), P(c_int)]),
     "b200_tiled_bytes": (c_u64, [c_int, c_int]),
     "b200_argmax_f32": (c_int, [c_vp, c_u64, c_int, c_int, c_u64]),
+    "b200_gemv_argmax_f32": (c_int, [c_vp, P(b200_qmat_t), c_u64, c_u64, c_int, c_u64]),
     "b200_capture_begin": (c_int, [c_vp]),
     "b200_capture_end": (c_int, [c_vp, P(c_vp)]),
     "b200_graph_launch": (c_int, [c_vp, c_vp]),

@@ -470,6 +470,7 @@ struct b200_engine {
     cudaEvent_t done;
     uint8_t *xscratch;  // quantised x for the two-kernel f32 path
     void *sel_scratch;  // argmax candidates
+    void *fsel_scratch; // fused greedy pick: per-CTA candidates + ticket
     b200_engine_config_t cfg;
 };
 
@@ -483,11 +484,13 @@ Tuning tuning_of(const b200_engine_config_t &c) {
     t.stages = c.stages;
     t.ctas_per_sm = c.ctas_per_sm;
     t.xreg_chunks = c.xreg_chunks;
+    t.kslices = c.kslices;
     return t;
 }
 
 // One engine GEMV: validate, then launch the kernel of W's layout.
-int engine_gemv(b200_engine_t *e, const b200_qmat_t *W, int xmode, const void *x, uint64_t y) {
+int engine_gemv(b200_engine_t *e, const b200_qmat_t *W, int xmode, const void *x, uint64_t y, int *sel_out = nullptr,
+                int sel_base = 0) {
     if (!e) return fail(kErrInval, "engine not open");
     if (!W) return fail(kErrInval, "null matrix");
     const char *why = nullptr;
@@ -502,6 +505,9 @@ int engine_gemv(b200_engine_t *e, const b200_qmat_t *W, int xmode, const void *x
         L.round_mode = e->cfg.round_mode;
         L.l2_policy = e->cfg.l2_policy;
         L.pdl = e->cfg.pdl != 0;
+        L.sel_out = sel_out;
+        L.sel_base = sel_base;
+        L.sel_scratch = e->fsel_scratch;
         if (tile_validate(L, &why)) return fail(kErrInval, "gemv %dx%d: %s", W->rows, W->k, why);
         if (int rc = use_device(e->device)) return rc;
         if (tile_launch(L, tuning_of(e->cfg), e->stream))
@@ -509,6 +515,7 @@ int engine_gemv(b200_engine_t *e, const b200_qmat_t *W, int xmode, const void *x
         return 0;
     }
     if (W->layout != B200_LAYOUT_ROWS) return fail(kErrInval, "unknown matrix layout %d", W->layout);
+    if (sel_out) return fail(kErrInval, "the fused greedy pick needs a tile-layout matrix");
     GemvLaunch L;
     L.region[0] = reinterpret_cast<const uint8_t *>(W->w);
     L.nregions = 1;
@@ -572,6 +579,8 @@ extern "C" int b200_engine_open(b200_engine_t **out, int device) {
     if (err == cudaSuccess) err = cudaEventCreateWithFlags(&e->done, cudaEventDisableTiming);
     if (err == cudaSuccess) err = cudaMalloc(reinterpret_cast<void **>(&e->xscratch), kXScratchBytes);
     if (err == cudaSuccess) err = cudaMalloc(&e->sel_scratch, static_cast<size_t>(argmax_scratch_bytes()));
+    if (err == cudaSuccess) err = cudaMalloc(&e->fsel_scratch, static_cast<size_t>(tile_select_scratch_bytes()));
+    if (err == cudaSuccess) err = cudaMemset(e->fsel_scratch, 0, static_cast<size_t>(tile_select_scratch_bytes()));
     if (err != cudaSuccess) {
         b200_engine_close(e);
         return cuda_fail(err, "engine set-up");
@@ -586,6 +595,7 @@ extern "C" int b200_engine_open(b200_engine_t **out, int device) {
     e->cfg.fuse_quantize = 0;
     e->cfg.prefetch_next = 0;
     e->cfg.xreg_chunks = 8;
+    e->cfg.kslices = 1;
     *out = e;
     return 0;
 }
@@ -597,6 +607,7 @@ extern "C" int b200_engine_close(b200_engine_t *e) {
     if (e->side) cudaStreamSynchronize(e->side);
     if (e->xscratch) cudaFree(e->xscratch);
     if (e->sel_scratch) cudaFree(e->sel_scratch);
+    if (e->fsel_scratch) cudaFree(e->fsel_scratch);
     if (e->fork) cudaEventDestroy(e->fork);
     if (e->done) cudaEventDestroy(e->done);
     if (e->side) cudaStreamDestroy(e->side);
@@ -617,6 +628,7 @@ extern "C" int b200_engine_set_config(b200_engine_t *e, const b200_engine_config
         return fail(kErrInval, "config out of range");
     if (cfg->l2_policy < 0 || cfg->l2_policy > 2 || cfg->round_mode < 0 || cfg->round_mode > 1)
         return fail(kErrInval, "config out of range");
+    if (cfg->kslices != 1 && cfg->kslices != 2 && cfg->kslices != 4) return fail(kErrInval, "kslices must be 1, 2 or 4");
     e->cfg = *cfg;
     return 0;
 }
@@ -660,6 +672,21 @@ extern "C" int b200_gemv_f32(b200_engine_t *e, const b200_qmat_t *W, uint64_t x,
     if (int rc = engine_gemv(e, W, kXF32, reinterpret_cast<const void *>(x), y)) return rc;
     if (next && e->cfg.prefetch_next) return prefetch_on_side(e, next);
     return 0;
+}
+
+extern "C" int b200_gemv_argmax_f32(b200_engine_t *e, const b200_qmat_t *W, uint64_t x, uint64_t y, int index_base,
+                                    uint64_t out) {
+    if (!e) return fail(kErrInval, "engine not open");
+    if (int rc = check_qmat(W)) return rc;
+    if (!out || out % 8) return fail(kErrInval, "out must be 8-byte aligned");
+    if (W->layout != B200_LAYOUT_TILES) return fail(kErrInval, "the fused greedy pick needs a tile-layout matrix");
+    int *sel = reinterpret_cast<int *>(out);
+    if (!e->cfg.fuse_quantize) {
+        if (x % 16) return fail(kErrInval, "x must be 16-byte aligned");
+        if (int rc = b200_quantize_q8_0(e, x, reinterpret_cast<uint64_t>(e->xscratch), W->k)) return rc;
+        return engine_gemv(e, W, kXPacked, e->xscratch, y, sel, index_base);
+    }
+    return engine_gemv(e, W, kXF32, reinterpret_cast<const void *>(x), y, sel, index_base);
 }
 
 extern "C" uint64_t b200_tiled_bytes(int rows, int k) { return static_cast<uint64_t>(tiled_bytes(rows, k)); }

@@ -24,64 +24,70 @@ __device__ __forceinline__ int q8_round(float s, int mode) {
     return s < 0.0f ? -m : m;
 }
 
-// One Q8_0 block held by 8 consecutive threads (4 values each). Returns this
-// thread's 4 int8 packed in a word; *d gets the float32 scale before rounding
-// to float16, *sum the block's int sum (all 8 threads get both).
-// q4_0.py:89-97: amax / 127, inv = d == 0 ? 0 : 1/d, both IEEE-rounded.
-__device__ __forceinline__ uint32_t q8_quant_group(float4 v, int mode, float *d, int *sum) {
-    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-    amax = fmaxf(amax, __shfl_xor_sync(kFullMask, amax, 1, 8));
-    amax = fmaxf(amax, __shfl_xor_sync(kFullMask, amax, 2, 8));
-    amax = fmaxf(amax, __shfl_xor_sync(kFullMask, amax, 4, 8));
+// One Q8_0 block quantised by one thread (q4_0.py:83-97): amax / 127,
+// inv = d == 0 ? 0 : 1/d (both IEEE-rounded), the contract's rounding per
+// value. Writes 8 int8x4 words to q; returns the int sum, *d the float32 scale.
+__device__ __forceinline__ int q8_quant_block(const float4 v[8], int mode, uint32_t q[8], float *d) {
+    float m[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m[j] = fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w)));
+    const float amax = fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
     const float db = __fdiv_rn(amax, 127.0f);
     const float inv = db == 0.0f ? 0.0f : __fdiv_rn(1.0f, db);
-    const int q0 = q8_round(__fmul_rn(v.x, inv), mode);
-    const int q1 = q8_round(__fmul_rn(v.y, inv), mode);
-    const int q2 = q8_round(__fmul_rn(v.z, inv), mode);
-    const int q3 = q8_round(__fmul_rn(v.w, inv), mode);
-    int s = q0 + q1 + q2 + q3;
-    s += __shfl_xor_sync(kFullMask, s, 1, 8);
-    s += __shfl_xor_sync(kFullMask, s, 2, 8);
-    s += __shfl_xor_sync(kFullMask, s, 4, 8);
+    int sum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int q0 = q8_round(__fmul_rn(v[j].x, inv), mode);
+        const int q1 = q8_round(__fmul_rn(v[j].y, inv), mode);
+        const int q2 = q8_round(__fmul_rn(v[j].z, inv), mode);
+        const int q3 = q8_round(__fmul_rn(v[j].w, inv), mode);
+        sum += q0 + q1 + q2 + q3;
+        q[j] = (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
+               ((static_cast<uint32_t>(q2) & 0xffu) << 16) | ((static_cast<uint32_t>(q3) & 0xffu) << 24);
+    }
     *d = db;
-    *sum = s;
-    return (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
-           ((static_cast<uint32_t>(q2) & 0xffu) << 16) | ((static_cast<uint32_t>(q3) & 0xffu) << 24);
+    return sum;
 }
 
 // x into shared memory for the whole CTA: int8[k] at xs, then (float32 d,
 // int32 sum of the 32 int8) per block at xs + k. `x` is float32[k] (quantised
 // here, q4_0.py:83-97) or the engine buffer int8[k] + float32[k/32].
-// Every thread of the CTA must call this (it shuffles in groups of 8).
+// One thread per block, all loads issued before any use and no shuffles, so
+// the staging costs one memory round trip plus one block's arithmetic; the
+// CTA must have at least k/32 threads.
 template <int XMODE>
 __device__ __forceinline__ void stage_x(const void *x, int k, int round_mode, uint8_t *xs) {
-    const int nb = k / kQK, per_pass = blockDim.x / 8;
-    for (int b0 = 0; b0 < nb; b0 += per_pass) {
-        const int b = b0 + static_cast<int>(threadIdx.x) / 8, sub = threadIdx.x % 8;
-        const bool ok = b < nb;
-        uint32_t packed = 0;
-        float d = 0.0f;
+    const int nb = k / kQK, b = threadIdx.x;
+    if (b >= nb) return;
+    uint4 *qdst = reinterpret_cast<uint4 *>(xs + 32 * b);
+    if constexpr (XMODE == kXF32) {
+        const float4 *src = reinterpret_cast<const float4 *>(x) + 8 * b;
+        float4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __ldg(src + j);
+        uint32_t q[8];
+        float d;
+        const int sum = q8_quant_block(v, round_mode, q, &d);
+        qdst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+        qdst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+        reinterpret_cast<int2 *>(xs + k)[b] = make_int2(__float_as_int(__half2float(__float2half_rn(d))), sum);
+    } else {
+        const uint8_t *xq = static_cast<const uint8_t *>(x);
+        const uint4 a = __ldg(reinterpret_cast<const uint4 *>(xq + 32 * b));
+        const uint4 c = __ldg(reinterpret_cast<const uint4 *>(xq + 32 * b) + 1);
+        const float d = __ldg(reinterpret_cast<const float *>(xq + k) + b);
         int sum = 0;
-        if constexpr (XMODE == kXF32) {
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (ok) v = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(x) + 32 * b) + sub);
-            packed = q8_quant_group(v, round_mode, &d, &sum);
-            d = __half2float(__float2half_rn(d));
-        } else {
-            const uint8_t *xq = static_cast<const uint8_t *>(x);
-            if (ok) {
-                packed = __ldg(reinterpret_cast<const uint32_t *>(xq + 32 * b) + sub);
-                d = __ldg(reinterpret_cast<const float *>(xq + k) + b);
-            }
-            sum = __dp4a(static_cast<int>(packed), 0x01010101, 0);
-            sum += __shfl_xor_sync(kFullMask, sum, 1, 8);
-            sum += __shfl_xor_sync(kFullMask, sum, 2, 8);
-            sum += __shfl_xor_sync(kFullMask, sum, 4, 8);
-        }
-        if (ok) {
-            reinterpret_cast<uint32_t *>(xs)[8 * b + sub] = packed;
-            if (sub == 0) reinterpret_cast<int2 *>(xs + k)[b] = make_int2(__float_as_int(d), sum);
-        }
+        sum = __dp4a(static_cast<int>(a.x), 0x01010101, sum);
+        sum = __dp4a(static_cast<int>(a.y), 0x01010101, sum);
+        sum = __dp4a(static_cast<int>(a.z), 0x01010101, sum);
+        sum = __dp4a(static_cast<int>(a.w), 0x01010101, sum);
+        sum = __dp4a(static_cast<int>(c.x), 0x01010101, sum);
+        sum = __dp4a(static_cast<int>(c.y), 0x01010101, sum);
+        sum = __dp4a(static_cast<int>(c.z), 0x01010101, sum);
+        sum = __dp4a(static_cast<int>(c.w), 0x01010101, sum);
+        qdst[0] = a;
+        qdst[1] = c;
+        reinterpret_cast<int2 *>(xs + k)[b] = make_int2(__float_as_int(d), sum);
     }
 }
 

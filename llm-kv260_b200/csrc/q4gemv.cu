@@ -200,6 +200,8 @@ __global__ void __launch_bounds__(kThreads, 1) q4_gemv_kernel(const __grid_const
     pdl_launch_dependents();
     pdl_wait_prior_grid();
 
+    // One thread per x block: 256 threads >= 8192 / 32 blocks.
+    static_assert(kThreads >= kMaxK / kQK, "stage_x needs a thread per x block");
     stage_x<XMODE>(p.x, p.k, p.round_mode, xs);
     __syncthreads();
 
@@ -215,23 +217,22 @@ __global__ void __launch_bounds__(kThreads, 1) q4_gemv_kernel(const __grid_const
     }
 }
 
-// x float32[k] -> int8[k] then float32[k/32]; 8 threads per block.
-__global__ void __launch_bounds__(256) q8_quantize_kernel(const float *__restrict__ x, uint8_t *__restrict__ out,
+// x float32[k] -> int8[k] then float32[k/32]; one thread per block.
+__global__ void __launch_bounds__(128) q8_quantize_kernel(const float *__restrict__ x, uint8_t *__restrict__ out,
                                                           int k, int round_mode) {
-    pdl_wait_prior_grid();
-    const int nb = k / kQK;
-    const int g = blockIdx.x * (blockDim.x / 8) + threadIdx.x / 8, sub = threadIdx.x % 8;
-    const bool ok = g < nb;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (ok) v = __ldg(reinterpret_cast<const float4 *>(x + 32 * g) + sub);
-    float d;
-    int sum;
-    const uint32_t packed = q8_quant_group(v, round_mode, &d, &sum);
-    if (ok) {
-        reinterpret_cast<uint32_t *>(out)[8 * g + sub] = packed;
-        if (sub == 0) reinterpret_cast<float *>(out + k)[g] = __half2float(__float2half_rn(d));
-    }
     pdl_launch_dependents();
+    pdl_wait_prior_grid();
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= k / kQK) return;
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __ldg(reinterpret_cast<const float4 *>(x) + 8 * b + j);
+    uint32_t q[8];
+    float d;
+    (void)q8_quant_block(v, round_mode, q, &d);
+    reinterpret_cast<uint4 *>(out)[2 * b] = make_uint4(q[0], q[1], q[2], q[3]);
+    reinterpret_cast<uint4 *>(out)[2 * b + 1] = make_uint4(q[4], q[5], q[6], q[7]);
+    reinterpret_cast<float *>(out + k)[b] = __half2float(__float2half_rn(d));
 }
 
 constexpr uint32_t kPrefetchChunk = 32768;
@@ -497,8 +498,8 @@ int quantize_launch(const float *x, uint8_t *xpacked, int k, int round_mode, cud
     if (round_mode != kRoundContract && round_mode != kRoundRoundf) return kErrInval;
     const int nb = k / kQK;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((nb + 31) / 32);
-    cfg.blockDim = dim3(256);
+    cfg.gridDim = dim3((nb + 127) / 128);
+    cfg.blockDim = dim3(128);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -55,6 +55,7 @@ struct Tuning {
     int stages = 4;           // stages in flight per CTA
     int ctas_per_sm = 2;      // grid = SMs x this, at most one CTA per stage
     int xreg_chunks = 8;      // rows of at most this many 144-byte chunks keep x in registers
+    int kslices = 1;          // tile kernel: split each row's chunks over at least this many thread slices (1, 2, 4)
 };
 
 // Error codes shared with the C ABI (negative errno values).
@@ -91,7 +92,12 @@ struct TileLaunch {
     int round_mode = kRoundContract;
     int l2_policy = kL2EvictFirst;
     bool pdl = false;
+    // optional fused greedy pick (see argmax_launch for the rule)
+    int *sel_out = nullptr;       // 8 bytes: int32 index + sel_base, float32 value
+    int sel_base = 0;
+    void *sel_scratch = nullptr;  // tile_select_scratch_bytes(), ticket zeroed once
 };
+int tile_select_scratch_bytes();
 
 size_t tiled_bytes(int rows, int k);  // 0 for an unusable shape
 int tile_validate(const TileLaunch &L, const char **why);

@@ -13,14 +13,19 @@
 // the low nibble, weight j+16 in the high one), so the bytes per weight stay
 // 18/32 and the algorithmic traffic is the GGUF file's.
 //
-// Kernel. 128 threads: thread t owns lane L = t / 16 (blocks 8c + L) of row
-// i = t % 16 and runs that lane's sequential float32 chain. A stage is a run
-// of whole tiles of one row group, moved by ONE 1-D bulk copy (TMA engine,
-// no multicast) into an mbarrier ring. Every block is one conflict-free
-// 128-bit shared load (a warp reads 512 contiguous bytes) plus a 16-bit
-// scale load, 8 __dp4a, two rounded multiplies and the lane add; all warps run
-// identical code. Per row group the 8 lane sums meet in tree_sum's order
-// through shared memory.
+// Kernel. A CTA owns whole 16-row groups. Thread (s, l, i) -- K-slice s,
+// lane l, row i -- computes the block terms of lane l of row i for the chunks
+// of slice s (at most 8, so its x blocks stay in registers). With one slice
+// (K <= 2048) the thread adds its terms straight into the lane chain; with
+// several, the terms go to shared memory and slice 0 then runs each lane's
+// chain over all chunks in order -- the float adds stay sequential exactly as
+// q4_0.py:177-179 orders them, only the block dots run in parallel. A stage is
+// one row group's whole tile run, moved by ONE 1-D bulk copy (TMA engine, no
+// multicast) into an mbarrier ring, issued before the kernel waits on its
+// predecessor (programmatic dependent launch). Every block is one conflict-
+// free 128-bit shared load (a warp reads 512 contiguous bytes) plus a 16-bit
+// scale load and 8 __dp4a; all warps run identical code. Per row group the 8
+// lane sums meet in tree_sum's order.
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -29,13 +34,14 @@ namespace b200 {
 
 namespace {
 
-constexpr int kTileThreads = kTileRows * kLanes;   // 128
+constexpr int kTileThreads = kTileRows * kLanes;   // threads per K-slice: 128
 constexpr int kTileNibBytes = kTileThreads * 16;   // 2048
 constexpr int kMaxStages = 8;
 constexpr int kBarBytes = 64;
 constexpr int kRedBytes = 2 * kTileThreads * 4;    // double-buffered lane sums
 constexpr int kSmemAlign = 128;
-constexpr int kXRegMaxChunks = 8;                  // x in registers up to K = 2048
+constexpr int kMaxCps = 8;                         // chunks per K-slice (x blocks in registers)
+constexpr int kSelMaxCtas = 4096;                  // fused greedy pick: candidate slots
 
 struct TileParams {
     const uint8_t *w;
@@ -44,42 +50,63 @@ struct TileParams {
     unsigned *status;
     int rows, k, nb, nch;
     int groups;
-    int cps;         // tiles (chunks) per stage
-    int slices;      // stages per row group
-    int slot_bytes;  // cps * 2304
+    int slot_bytes;  // nch * 2304: one row group
     int stages;
     int round_mode;
     int l2_policy;
+    // Optional greedy pick over y, fused (tp_llama.cpp:879-882): when sel_out
+    // is set, every CTA posts its best (value, row) to sel_cand[blockIdx.x],
+    // and the last CTA to finish reduces them into sel_out (int32 index +
+    // sel_base, then float32 value) and resets the ticket to 0.
+    int *sel_out;
+    int sel_base;
+    float2 *sel_cand;    // gridDim.x entries: (value, row as float bits)
+    unsigned *sel_ticket;
 };
 
-__device__ __forceinline__ void issue_tile_stage(const TileParams &p, uint64_t *bars, uint8_t *ring, int g0, int s,
-                                                 uint64_t policy) {
-    const int g = g0 + s / p.slices, c0 = (s % p.slices) * p.cps;
-    const int cc = min(p.cps, p.nch - c0);
-    const int slot = s % p.stages;
-    const uint32_t bytes = static_cast<uint32_t>(cc * kTileBytes);
-    mbar_arrive_expect_tx(&bars[slot], bytes);
-    bulk_g2s(ring + slot * p.slot_bytes, p.w + (static_cast<size_t>(g) * p.nch + c0) * kTileBytes, bytes, &bars[slot],
-             policy);
+// (value desc, index asc); NaN never beats a number (the scan's rule for any
+// index but 0, which the final step handles).
+__device__ __forceinline__ bool sel_better(float av, int ai, float bv, int bi) {
+    if (isnan(bv)) return !isnan(av) || ai < bi;
+    if (isnan(av)) return false;
+    return av > bv || (av == bv && ai < bi);
 }
 
-// NCH > 0: x in registers and a stage holds whole rows (K = 256 * NCH).
-// NCH == 0: x read per block from shared memory, stages of p.cps tiles.
-template <int XMODE, int NCH>
-__global__ void __launch_bounds__(kTileThreads) q4_tile_kernel(const __grid_constant__ TileParams p) {
+__device__ __forceinline__ void issue_group(const TileParams &p, uint64_t *bars, uint8_t *ring, int g, int s,
+                                            uint64_t policy) {
+    const int slot = s % p.stages;
+    mbar_arrive_expect_tx(&bars[slot], static_cast<uint32_t>(p.slot_bytes));
+    bulk_g2s(ring + slot * p.slot_bytes, p.w + static_cast<size_t>(g) * p.slot_bytes,
+             static_cast<uint32_t>(p.slot_bytes), &bars[slot], policy);
+}
+
+// Block term of tile `tile` (one chunk of the row group) for this thread's
+// (lane, row) slot u = lane * 16 + row.
+__device__ __forceinline__ float tile_term(const uint8_t *tile, int u, const XBlock &xb) {
+    const uint4 nv = *reinterpret_cast<const uint4 *>(tile + u * 16);
+    const uint32_t db = *reinterpret_cast<const uint16_t *>(tile + kTileNibBytes + u * 2);
+    const uint32_t n[4] = {nv.x, nv.y, nv.z, nv.w};
+    return block_term_words(n, db, xb);
+}
+
+// CPS: chunks per K-slice; KS: K-slices (threads = 128 * KS); KS * CPS >= nch.
+template <int XMODE, int CPS, int KS>
+__global__ void __launch_bounds__(kTileThreads * KS) q4_tile_kernel(const __grid_constant__ TileParams p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ int s_abort;
     uint8_t *ring = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + kSmemAlign - 1) & ~static_cast<uintptr_t>(kSmemAlign - 1));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + p.stages * p.slot_bytes);
-    float *red = reinterpret_cast<float *>(ring + p.stages * p.slot_bytes + kBarBytes);
-    uint8_t *xs = ring + p.stages * p.slot_bytes + kBarBytes + kRedBytes;
+    uint8_t *after = ring + p.stages * p.slot_bytes;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(after);
+    float *red = reinterpret_cast<float *>(after + kBarBytes);
+    float *tv = reinterpret_cast<float *>(after + kBarBytes + kRedBytes);  // [nch][128], KS > 1 only
+    uint8_t *xs = after + kBarBytes + kRedBytes + (KS > 1 ? p.nch * kTileThreads * 4 : 0);
 
-    const int t = threadIdx.x, L = t / kTileRows;
+    const int t = threadIdx.x, slice = t / kTileThreads, u = t % kTileThreads, L = u / kTileRows;
     const int g0 = static_cast<int>(static_cast<long long>(p.groups) * blockIdx.x / gridDim.x);
     const int g1 = static_cast<int>(static_cast<long long>(p.groups) * (blockIdx.x + 1) / gridDim.x);
     const int S = p.stages;
-    const int nst = (g1 - g0) * p.slices;
+    const int nst = g1 - g0;
 
     if (t == 0) {
         s_abort = 0;
@@ -91,65 +118,120 @@ __global__ void __launch_bounds__(kTileThreads) q4_tile_kernel(const __grid_cons
     // The weights do not depend on the previous kernel: start them moving,
     // let the next kernel launch, then wait for x.
     if (t == 0)
-        for (int s = 0; s < nst && s < S; ++s) issue_tile_stage(p, bars, ring, g0, s, policy);
+        for (int s = 0; s < nst && s < S; ++s) issue_group(p, bars, ring, g0 + s, s, policy);
     pdl_launch_dependents();
     pdl_wait_prior_grid();
 
+    // One thread per x block: 128*KS threads >= 8*nch blocks, as KS >= nch/8.
     stage_x<XMODE>(p.x, p.k, p.round_mode, xs);
     __syncthreads();
-    XBlock xr[NCH > 0 ? NCH : 1];
-    if constexpr (NCH > 0) {
+    const int c_first = slice * CPS;
+    XBlock xr[CPS];
 #pragma unroll
-        for (int c = 0; c < NCH; ++c) load_xblock_smem(xs, p.k, 8 * c + L, xr[c]);
-    }
+    for (int j = 0; j < CPS; ++j)
+        if (c_first + j < p.nch) load_xblock_smem(xs, p.k, 8 * (c_first + j) + L, xr[j]);
 
-    float acc = 0.0f;
+    float best_v = __int_as_float(0x7fc00000);  // NaN: loses to any number
+    int best_i = 0x7fffffff;
     int s = 0;
     for (; s < nst; ++s) {
-        const int slot = s % S, gi = s / p.slices, sl = s % p.slices;
+        const int slot = s % S;
         if (!wait_stage(&bars[slot], static_cast<uint32_t>((s / S) & 1), p.status)) s_abort = 1;
-        const uint8_t *tile = ring + slot * p.slot_bytes;
-        if constexpr (NCH > 0) {
+        const uint8_t *tiles = ring + slot * p.slot_bytes;
+        float *rbuf = red + (s & 1) * kTileThreads;
+        if constexpr (KS == 1) {
+            float acc = 0.0f;
 #pragma unroll
-            for (int c = 0; c < NCH; ++c) {
-                const uint4 nv = *reinterpret_cast<const uint4 *>(tile + c * kTileBytes + t * 16);
-                const uint32_t db = *reinterpret_cast<const uint16_t *>(tile + c * kTileBytes + kTileNibBytes + t * 2);
-                const uint32_t n[4] = {nv.x, nv.y, nv.z, nv.w};
-                acc = __fadd_rn(acc, block_term_words(n, db, xr[c]));
-            }
+            for (int j = 0; j < CPS; ++j)
+                if (j < p.nch) acc = __fadd_rn(acc, tile_term(tiles + j * kTileBytes, u, xr[j]));
+            rbuf[u] = acc;
         } else {
-            const int c0 = sl * p.cps, cc = min(p.cps, p.nch - c0);
-#pragma unroll 2
-            for (int j = 0; j < cc; ++j) {
-                const uint4 nv = *reinterpret_cast<const uint4 *>(tile + j * kTileBytes + t * 16);
-                const uint32_t db = *reinterpret_cast<const uint16_t *>(tile + j * kTileBytes + kTileNibBytes + t * 2);
-                const uint32_t n[4] = {nv.x, nv.y, nv.z, nv.w};
-                XBlock xb;
-                load_xblock_smem(xs, p.k, 8 * (c0 + j) + L, xb);
-                acc = __fadd_rn(acc, block_term_words(n, db, xb));
+#pragma unroll
+            for (int j = 0; j < CPS; ++j) {
+                const int c = c_first + j;
+                if (c < p.nch) tv[c * kTileThreads + u] = tile_term(tiles + c * kTileBytes, u, xr[j]);
             }
-        }
-        const bool last_slice = sl == p.slices - 1;
-        float *rbuf = red + (gi & 1) * kTileThreads;
-        if (last_slice) {
-            rbuf[t] = acc;  // [lane][row]
-            acc = 0.0f;
+            __syncthreads();
+            if (slice == 0) {
+                // lane chain over all chunks, in order (q4_0.py:177-179)
+                float acc = 0.0f;
+                for (int c = 0; c < p.nch; ++c) acc = __fadd_rn(acc, tv[c * kTileThreads + u]);
+                rbuf[u] = acc;
+            }
         }
         __syncthreads();
         if (s_abort) break;
-        if (t == 0 && s + S < nst) issue_tile_stage(p, bars, ring, g0, s + S, policy);
-        if (last_slice && t < kTileRows) {
+        if (t == 0 && s + S < nst) issue_group(p, bars, ring, g0 + s + S, s + S, policy);
+        if (t < kTileRows) {
             const float *r = rbuf + t;
             const float yv = tree8(r[0 * kTileRows], r[1 * kTileRows], r[2 * kTileRows], r[3 * kTileRows],
                                    r[4 * kTileRows], r[5 * kTileRows], r[6 * kTileRows], r[7 * kTileRows]);
-            const int row = (g0 + gi) * kTileRows + t;
-            if (row < p.rows) p.y[row] = yv;
+            const int row = (g0 + s) * kTileRows + t;
+            if (row < p.rows) {
+                p.y[row] = yv;
+                if (sel_better(yv, row, best_v, best_i)) {
+                    best_v = yv;
+                    best_i = row;
+                }
+            }
+        }
+    }
+    if (p.sel_out) {
+        // CTA best over the 16 tree threads (lanes 0..15 of warp 0), then the
+        // last CTA to finish reduces all CTAs' bests.
+        if (t < 32) {
+            for (int off = 8; off > 0; off >>= 1) {
+                const float ov = __shfl_down_sync(kFullMask, best_v, off, 16);
+                const int oi = __shfl_down_sync(kFullMask, best_i, off, 16);
+                if (sel_better(ov, oi, best_v, best_i)) {
+                    best_v = ov;
+                    best_i = oi;
+                }
+            }
+        }
+        __shared__ unsigned s_last;
+        if (t == 0) {
+            p.sel_cand[blockIdx.x] = make_float2(best_v, __int_as_float(best_i));
+            __threadfence();
+            s_last = atomicAdd(p.sel_ticket, 1u) == gridDim.x - 1;
+        }
+        __syncthreads();
+        if (s_last && t < 32) {
+            __threadfence();
+            float bv = __int_as_float(0x7fc00000);
+            int bi = 0x7fffffff;
+            for (int c = t; c < static_cast<int>(gridDim.x); c += 32) {
+                const float2 cd = __ldcg(&p.sel_cand[c]);
+                if (sel_better(cd.x, __float_as_int(cd.y), bv, bi)) {
+                    bv = cd.x;
+                    bi = __float_as_int(cd.y);
+                }
+            }
+            for (int off = 16; off > 0; off >>= 1) {
+                const float ov = __shfl_down_sync(kFullMask, bv, off);
+                const int oi = __shfl_down_sync(kFullMask, bi, off);
+                if (sel_better(ov, oi, bv, bi)) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+            if (t == 0) {
+                const float y0 = __ldcg(p.y);
+                if (isnan(y0) || bi == 0x7fffffff) {  // the scan never leaves index 0 if y[0] is NaN
+                    bv = y0;
+                    bi = 0;
+                }
+                p.sel_out[0] = bi + p.sel_base;
+                p.sel_out[1] = __float_as_int(bv);
+                *p.sel_ticket = 0;
+            }
         }
     }
     if (s < nst && t == 0) {
         // Aborted on a stage timeout: let copies already in flight land (each
         // wait bounded) before the CTA's shared memory goes away.
-        for (int r = s; r < nst && r < s + S; ++r) (void)wait_stage(&bars[r % S], static_cast<uint32_t>((r / S) & 1), p.status);
+        for (int r = s; r < nst && r < s + S; ++r)
+            (void)wait_stage(&bars[r % S], static_cast<uint32_t>((r / S) & 1), p.status);
     }
 }
 
@@ -180,19 +262,27 @@ __global__ void repack_tiles_kernel(const uint8_t *__restrict__ src, int rows, i
 
 using TileKernelFn = void (*)(TileParams);
 
-template <int XMODE>
-TileKernelFn pick_tile(int nch_reg) {
-    switch (nch_reg) {
-        case 1: return q4_tile_kernel<XMODE, 1>;
-        case 2: return q4_tile_kernel<XMODE, 2>;
-        case 3: return q4_tile_kernel<XMODE, 3>;
-        case 4: return q4_tile_kernel<XMODE, 4>;
-        case 5: return q4_tile_kernel<XMODE, 5>;
-        case 6: return q4_tile_kernel<XMODE, 6>;
-        case 7: return q4_tile_kernel<XMODE, 7>;
-        case 8: return q4_tile_kernel<XMODE, 8>;
-        default: return q4_tile_kernel<XMODE, 0>;
+template <int XMODE, int KS>
+TileKernelFn pick_cps(int cps) {
+    switch (cps) {
+        case 1: return q4_tile_kernel<XMODE, 1, KS>;
+        case 2: return q4_tile_kernel<XMODE, 2, KS>;
+        case 3: return q4_tile_kernel<XMODE, 3, KS>;
+        case 4: return q4_tile_kernel<XMODE, 4, KS>;
+        case 5: return q4_tile_kernel<XMODE, 5, KS>;
+        case 6: return q4_tile_kernel<XMODE, 6, KS>;
+        case 7: return q4_tile_kernel<XMODE, 7, KS>;
+        case 8: return q4_tile_kernel<XMODE, 8, KS>;
+        default: return nullptr;
     }
+}
+
+template <int XMODE>
+TileKernelFn pick_tile(int cps, int ks) {
+    if (ks == 1) return pick_cps<XMODE, 1>(cps);
+    if (ks == 2) return pick_cps<XMODE, 2>(cps);
+    if (ks == 4) return pick_cps<XMODE, 4>(cps);
+    return nullptr;
 }
 
 struct TilePlan {
@@ -200,14 +290,21 @@ struct TilePlan {
     TileKernelFn fn;
     int grid;
     int smem;
+    int threads;
 };
 
 int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
     const char *why = nullptr;
     if (int rc = tile_validate(L, &why)) return rc;
     const int nb = L.k / kQK, nch = nb / kLanes;
-    const bool xreg = nch <= tu.xreg_chunks && nch <= kXRegMaxChunks;
-    TileKernelFn fn = L.xmode == kXF32 ? pick_tile<kXF32>(xreg ? nch : 0) : pick_tile<kXPacked>(xreg ? nch : 0);
+    // K-slices: enough that a slice has at most 8 chunks, more if asked.
+    int ks = 1;
+    while (ks < 4 && (ks * kMaxCps < nch || ks < tu.kslices)) ks *= 2;
+    while (ks > 1 && ks > nch) ks /= 2;  // every slice gets at least one chunk
+    const int cps = (nch + ks - 1) / ks;
+    if (cps > kMaxCps) return kErrInval;
+    TileKernelFn fn = L.xmode == kXF32 ? pick_tile<kXF32>(cps, ks) : pick_tile<kXPacked>(cps, ks);
+    if (!fn) return kErrInval;
     TileParams p{};
     p.w = L.w;
     p.y = L.y;
@@ -219,17 +316,20 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
     p.nb = nb;
     p.nch = nch;
     p.groups = (L.rows + kTileRows - 1) / kTileRows;
-    int cps = xreg ? nch : tu.stage_bytes / kTileBytes;
-    if (cps < 1) cps = 1;
-    if (cps > nch) cps = nch;
-    p.cps = cps;
-    p.slices = (nch + cps - 1) / cps;
-    p.slot_bytes = cps * kTileBytes;
+    p.slot_bytes = nch * kTileBytes;
     p.stages = tu.stages < 1 ? 1 : (tu.stages > kMaxStages ? kMaxStages : tu.stages);
     p.round_mode = L.round_mode;
     p.l2_policy = L.l2_policy;
+    if (L.sel_out) {
+        if (!L.sel_scratch) return kErrInval;
+        p.sel_out = L.sel_out;
+        p.sel_base = L.sel_base;
+        p.sel_cand = static_cast<float2 *>(L.sel_scratch);
+        p.sel_ticket = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(L.sel_scratch) + kSelMaxCtas * sizeof(float2));
+    }
+    const int threads = kTileThreads * ks;
     const int xarea = round_up(L.k + 8 * nb, 16);
-    const int fixed = kSmemAlign + kBarBytes + kRedBytes + xarea;
+    const int fixed = kSmemAlign + kBarBytes + kRedBytes + (ks > 1 ? nch * kTileThreads * 4 : 0) + xarea;
     const int limit = max_smem_optin();
     while (p.stages > 1 && fixed + p.stages * p.slot_bytes > limit) p.stages -= 1;
     const int smem = fixed + p.stages * p.slot_bytes;
@@ -237,18 +337,22 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
     const int sms = sm_count();
     if (sms <= 0) return kErrNoDev;
     int per_sm = tu.ctas_per_sm < 1 ? 1 : tu.ctas_per_sm;
-    const int fit = resident_ctas(reinterpret_cast<const void *>(fn), kTileThreads, smem);
+    const int fit = resident_ctas(reinterpret_cast<const void *>(fn), threads, smem);
     if (per_sm > fit) per_sm = fit;  // one wave: every CTA resident at once
     int grid = sms * per_sm;
     if (grid > p.groups) grid = p.groups;
+    if (grid > kSelMaxCtas) grid = kSelMaxCtas;
     out->p = p;
     out->fn = fn;
     out->grid = grid;
     out->smem = smem;
+    out->threads = threads;
     return 0;
 }
 
 }  // namespace
+
+int tile_select_scratch_bytes() { return static_cast<int>(kSelMaxCtas * sizeof(float2) + 16); }
 
 size_t tiled_bytes(int rows, int k) {
     if (rows <= 0 || k <= 0 || k % 256) return 0;
@@ -282,7 +386,7 @@ int tile_launch(const TileLaunch &L, const Tuning &tu, cudaStream_t stream) {
     if (!ensure_smem(reinterpret_cast<const void *>(pl.fn), pl.smem)) return kErrCuda;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(pl.grid);
-    cfg.blockDim = dim3(kTileThreads);
+    cfg.blockDim = dim3(pl.threads);
     cfg.dynamicSmemBytes = static_cast<size_t>(pl.smem);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];

@@ -135,6 +135,11 @@ class Engine:
         check(lib().b200_repack_q4_0(self.h, W.c.w, W.rows, W.k, dev_ptr(dst)), "b200_repack_q4_0")
         return QMat(dst, W.rows, W.k, LAYOUT_TILES)
 
+    def gemv_argmax_f32(self, W: QMat, x, y, out, index_base: int = 0) -> None:
+        """gemv_f32 with the greedy pick over y fused into it (out: int32 index + index_base, float32 value)."""
+        check(lib().b200_gemv_argmax_f32(self.h, ctypes.byref(W.c), dev_ptr(x), dev_ptr(y), index_base, dev_ptr(out)),
+              "b200_gemv_argmax_f32")
+
     def argmax(self, y, n: int, out, index_base: int = 0) -> None:
         """First index of the largest of y[:n] (+ index_base) and its value -> out (8 bytes: int32, float32)."""
         check(lib().b200_argmax_f32(self.h, dev_ptr(y), n, index_base, dev_ptr(out)), "b200_argmax_f32")

@@ -104,3 +104,29 @@ def test_graph_replay_matches_eager_calls(torch_mod, pkg, oracle):
     assert np.array_equal(host.numpy().view(np.uint32), want_y2.view(np.uint32))
     g.close()
     e.close()
+
+
+@pytest.mark.parametrize("rows", [1, 17, 2048, 16032])
+@pytest.mark.parametrize("fuse", [0, 1])
+def test_fused_greedy_pick_matches_gemv_then_scan(torch_mod, pkg, eng, oracle, rows, fuse):
+    """lm_head GEMV with the pick fused in: y bit-exact, pick = the runtime's scan of y."""
+    torch = torch_mod
+    k = 2048
+    w = cases.std_weights(rows, k, 300 + rows)
+    if rows > 40:
+        w[rows // 2] = w[rows // 3]            # two equal rows: equal logits, the lower index wins
+    blocks = oracle.quantize_q4_0(w)
+    x = cases.std_weights(1, k, 301)[0]
+    want = oracle.gemv_q4_0_f32(blocks, k, x)
+    W = eng.repack(pkg.QMat(torch.from_numpy(blocks.reshape(-1).copy()).cuda(), rows, k))
+    eng.configure(fuse_quantize=fuse)
+    y = torch.empty(rows, device="cuda")
+    out = torch.zeros(2, dtype=torch.int32, device="cuda")
+    for _ in range(3):                          # the ticket resets itself between calls
+        eng.gemv_argmax_f32(W, torch.from_numpy(x).cuda(), y, out, index_base=1000)
+        eng.sync()
+        o = out.cpu().numpy()
+        assert np.array_equal(y.cpu().numpy().view(np.uint32), want.view(np.uint32))
+        assert int(o[0]) - 1000 == _scan(want)
+        assert o[1:2].view(np.float32)[0] == want[_scan(want)]
+    eng.configure(fuse_quantize=0)

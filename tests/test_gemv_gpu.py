@@ -56,7 +56,7 @@ def _run_engine(torch, pkg, eng, blocks, k, x, fuse=0, packed=False, oracle=None
         eng.gemv_f32(W, torch.from_numpy(x).cuda(), y)
     eng.sync()
     out = y.cpu().numpy()
-    eng.configure(fuse_quantize=0, stage_bytes=16384, stages=4, ctas_per_sm=2, xreg_chunks=8)
+    eng.configure(fuse_quantize=0, stage_bytes=16384, stages=4, ctas_per_sm=2, xreg_chunks=8, kslices=1)
     return out
 
 
@@ -128,23 +128,21 @@ def test_every_team_width_and_blocks_per_thread(torch_mod, pkg, eng, oracle, k, 
     blocks = oracle.quantize_q4_0(cases.std_weights(rows, k, 1000 + k + rows))
     x = cases.std_weights(1, k, 2000 + k)[0]
     want = oracle.gemv_q4_0_f32(blocks, k, x)
-    for layout in (0, 1):
-        for fuse in (0, 1):
-            for xreg in (0, 8):
-                got = _run_engine(torch_mod, pkg, eng, blocks, k, x, fuse=fuse, layout=layout, xreg_chunks=xreg)
-                assert np.array_equal(_bits(got), _bits(want)), f"k={k} rows={rows} fuse={fuse} layout={layout}"
+    for layout, fuse, ks in [(0, 0, 1), (0, 1, 1), (1, 0, 1), (1, 1, 1), (1, 0, 2), (1, 1, 4)]:
+        got = _run_engine(torch_mod, pkg, eng, blocks, k, x, fuse=fuse, layout=layout, kslices=ks)
+        assert np.array_equal(_bits(got), _bits(want)), f"k={k} rows={rows} fuse={fuse} layout={layout} ks={ks}"
 
 
 @pytest.mark.parametrize("layout", [0, 1])
 @pytest.mark.parametrize("k", [2048, 8192])
-@pytest.mark.parametrize("stage_bytes,stages,ctas,xreg", [(16, 1, 1, 0), (1152, 2, 1, 0), (4096, 3, 4, 8),
-                                                          (65536, 2, 2, 0), (16384, 8, 2, 8), (200000, 1, 1, 0)])
-def test_pipeline_shapes_do_not_change_bits(torch_mod, pkg, eng, oracle, stage_bytes, stages, ctas, xreg, k, layout):
+@pytest.mark.parametrize("stage_bytes,stages,ctas,ks", [(16, 1, 1, 1), (1152, 2, 1, 2), (4096, 3, 4, 4),
+                                                        (65536, 2, 2, 1), (16384, 8, 2, 2), (200000, 1, 1, 4)])
+def test_pipeline_shapes_do_not_change_bits(torch_mod, pkg, eng, oracle, stage_bytes, stages, ctas, ks, k, layout):
     blocks = oracle.quantize_q4_0(cases.std_weights(1000, k, 31))
     x = cases.std_weights(1, k, 32)[0]
     want = oracle.gemv_q4_0_f32(blocks, k, x)
     got = _run_engine(torch_mod, pkg, eng, blocks, k, x, stage_bytes=stage_bytes, stages=stages, ctas_per_sm=ctas,
-                      xreg_chunks=xreg, layout=layout)
+                      kslices=ks, layout=layout)
     assert np.array_equal(_bits(got), _bits(want))
 
 
