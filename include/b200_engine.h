@@ -113,6 +113,21 @@ B200_API int b200_graph_destroy(b200_graph_t *g);
  * (unified addressing); host memory should be pinned. */
 B200_API int b200_copy_async(b200_engine_t *e, uint64_t dst, uint64_t src, uint64_t bytes);
 
+/* The greedy pick of b200_argmax_f32 for callers that cannot allocate device
+ * memory. No counterpart in the reference: its engine had no allocator of
+ * its own. Opening an engine calls cudaMalloc; this entry point needs no
+ * engine and allocates nothing, so it serves code that runs during stream
+ * capture, callers whose device memory all comes from their own allocator,
+ * and processes where allocating after start-up is not allowed. Its scratch
+ * is a fixed 8 KB array inside the library (1024 per-CTA candidates) that
+ * every GPU loading the library holds until exit. Runs on the current
+ * device, on `stream` (NULL: the legacy default stream); y holds n floats,
+ * n <= 33554432 (larger n is refused with -EINVAL); out gets the int32 index
+ * + index_base, then the float32 value. The first call on a device looks up
+ * the array's device address, so make it before any stream capture. All
+ * calls share the array: calls that overlap on the GPU race. */
+B200_API int b200_argmax_f32_noalloc(uint64_t y, int n, int index_base, uint64_t out, void *stream);
+
 /* Block until the engine's queued work is done (bounded; -ETIMEDOUT). */
 B200_API int b200_engine_sync(b200_engine_t *e, int timeout_ms);
 /* Device status word (see gemv_dev_status); reading clears it. */

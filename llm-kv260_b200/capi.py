@@ -91,6 +91,7 @@ SIGNATURES: dict[str, tuple] = {
     "b200_gemv_plan": (c_int, [c_vp, c_int, c_int, c_int, c_int, P(c_int), P(c_int)]),
     "b200_tiled_bytes": (c_u64, [c_int, c_int]),
     "b200_argmax_f32": (c_int, [c_vp, c_u64, c_int, c_int, c_u64]),
+    "b200_argmax_f32_noalloc": (c_int, [c_u64, c_int, c_int, c_u64, c_vp]),
     "b200_gemv_argmax_f32": (c_int, [c_vp, P(b200_qmat_t), c_u64, c_u64, c_int, c_u64]),
     "b200_capture_begin": (c_int, [c_vp]),
     "b200_capture_end": (c_int, [c_vp, P(c_vp)]),

@@ -118,6 +118,12 @@ int launch_and_record(gemv_dev_t *d, const GemvLaunch &L) {
 
 }  // namespace
 
+namespace b200 {
+// Lets the other translation units of this library leave a message for
+// b200_last_error() / gemv_dev_last_error().
+int report_error(int code, const char *msg) { return fail(code, "%s", msg); }
+}  // namespace b200
+
 // =================================================================== gemv_dev.h
 
 extern "C" int gemv_dev_open_named(gemv_dev_t *d, const char *name, int quiet) {

@@ -116,6 +116,8 @@ int argmax_launch(const float *y, int n, int index_base, void *scratch, int *out
                   cudaStream_t stream, bool pdl);
 
 int read_status(unsigned *status);   // device status word of the current device
+// Record `msg` as the calling thread's last error; returns code.
+int report_error(int code, const char *msg);
 int clear_status();
 
 // Grid the GEMV would launch (for the bench's roofline accounting).

@@ -12,7 +12,10 @@
 
 #include <cmath>
 #include <cstdint>
+#include <cstdio>
+#include <mutex>
 
+#include "../../include/b200_engine.h"
 #include "common.cuh"
 
 namespace b200 {
@@ -116,4 +119,82 @@ int argmax_launch(const float *y, int n, int index_base, void *scratch, int *out
     return 0;
 }
 
+// ---------------------------------------------------------------------------
+// The greedy pick for callers that cannot allocate device memory.
+//
+// b200_argmax_f32 needs an engine, and opening an engine calls cudaMalloc
+// for its scratch. Some callers cannot do that: code that runs while a CUDA
+// graph is being captured, a caller whose memory is handed out by its own
+// pool or allocator (and must not see a second one), or a host that loads
+// this library into a process where device allocation is forbidden after
+// start-up. b200_argmax_f32_noalloc gives them the same pick with no
+// allocation at all: its scratch (one (value, index) candidate per CTA of
+// the first pass, 1024 of them, 8 KB) is the file-scope array below, which
+// every GPU that loads the library holds until the process exits.
+//
+// In host code `g_noalloc_cand` is only a stand-in for the symbol, not a
+// device address: passing it to a kernel would fault, or where the GPU can
+// reach host memory, silently use the wrong memory. So the first call on a
+// device, with that device current, asks cudaGetSymbolAddress for the real
+// address and keeps it for that device; later calls reuse it. Because of
+// that look-up, make the first call on each device before any stream
+// capture.
+//
+// Every call shares the one array and it keeps the last call's contents.
+// Nothing in it has to start at zero: a call writes every candidate it
+// reads. Calls whose kernels overlap on the GPU (different streams, or
+// different host threads) race on the array; run them one at a time.
+// ---------------------------------------------------------------------------
+
+namespace {
+
+constexpr int kNoAllocParts = kArgmaxMaxParts;  // candidate slots
+constexpr int kNoAllocMaxN = 1 << 25;           // largest y accepted: 33,554,432 floats
+
+static __device__ __align__(256) Cand g_noalloc_cand[kNoAllocParts];
+
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[64] = {};
+
+}  // namespace
+
 }  // namespace b200
+
+extern "C" int b200_argmax_f32_noalloc(uint64_t y, int n, int index_base, uint64_t out, void *stream) {
+    using namespace b200;
+    if (!y || !out || y % 4 || out % 4)
+        return report_error(kErrInval, "argmax (no-alloc): y and out must be non-null and 4-byte aligned");
+    if (n <= 0) return report_error(kErrInval, "argmax (no-alloc): n must be positive");
+    if (n > kNoAllocMaxN) {
+        char msg[160];
+        snprintf(msg, sizeof msg, "argmax (no-alloc): n = %d is above the limit of %d elements", n, kNoAllocMaxN);
+        return report_error(kErrInval, msg);
+    }
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return report_error(kErrNoDev, "argmax (no-alloc): no usable current CUDA device");
+    void *scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void *p = nullptr;
+            const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_cand);
+            if (err != cudaSuccess || !p) {
+                char msg[200];
+                snprintf(msg, sizeof msg, "argmax (no-alloc): cudaGetSymbolAddress failed on device %d: %s", dev,
+                         cudaGetErrorString(err));
+                return report_error(kErrCuda, msg);
+            }
+            g_noalloc_ptr[dev] = p;
+        }
+        scratch = g_noalloc_ptr[dev];
+    }
+    int *oi = reinterpret_cast<int *>(out);
+    if (argmax_launch(reinterpret_cast<const float *>(y), n, index_base, scratch, oi, reinterpret_cast<float *>(oi + 1),
+                      static_cast<cudaStream_t>(stream), false)) {
+        char msg[200];
+        snprintf(msg, sizeof msg, "argmax (no-alloc): launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return report_error(kErrCuda, msg);
+    }
+    return 0;
+}
