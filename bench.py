@@ -276,7 +276,8 @@ class TokenChain:
         self.y_gu = torch.empty(2 * self.s["ff_rows"], **f32)
         self.y_down = torch.empty(e, **f32)
         self.logits = torch.empty(self.s["vocab_rows"], **f32)
-        self.sel = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.sel_local = torch.zeros(2, dtype=torch.int32, device=dev)   # this rank's pick over its vocab shard
+        self.sel = torch.zeros(2, dtype=torch.int32, device=dev)         # the pick over all ranks
         self.x0_host = torch.from_numpy(np.random.default_rng(7).standard_normal(e).astype(np.float32)).pin_memory()
         self.sel_host = torch.zeros(2, dtype=torch.int32).pin_memory()
         self.x0.copy_(self.x0_host)
@@ -311,7 +312,11 @@ class TokenChain:
             self.allreduce(self.y_down)
             h = self.y_down
         _, Wlm = next(it)
-        e.gemv_argmax_f32(Wlm, h, self.logits, self.sel, index_base=self.rank * Wlm.rows)
+        if self.world > 1:
+            e.gemv_argmax_f32(Wlm, h, self.logits, self.sel_local, index_base=self.rank * Wlm.rows)
+            self.comm.pick(self.sel_local, self.sel)   # sample_token's candidate exchange, greedy
+        else:
+            e.gemv_argmax_f32(Wlm, h, self.logits, self.sel, index_base=0)
 
     def capture(self) -> None:
         self.token()                     # first calls set up the caches the capture needs
@@ -415,12 +420,14 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     for _ in range(args.warmup):
         chain.step()
     chain.stream.synchronize()
-    barrier(world)
-    torch.cuda.synchronize()
+    # the sampler starts before the barrier: a rank that entered the timed
+    # region early would otherwise time its peers' start-up in the all-reduces
     sampler = ClockSampler(local_rank) if rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.15)
+    barrier(world)
+    torch.cuda.synchronize()
     ms = timed(torch, chain.stream, chain.step, args.steps, flush)
     torch.cuda.synchronize()
     clocks = sampler.stop() if sampler else None
@@ -451,7 +458,9 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
             rate, n, cores = cpu_rate(mats_host, chain.x0_host.numpy(), budget_s=10.0)
             cpu = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
                    "sample": f"{n} whole tokens of the same chain through the C oracle (10 s budget)"}
-        kernels_per_step = len(chain.mats)  # one GEMV kernel each; the greedy pick is fused into lm_head
+        # one GEMV kernel each (the greedy pick is fused into lm_head); at N > 1 also
+        # 2 all-reduce kernels per layer and the candidate exchange
+        kernels_per_step = len(chain.mats) + (2 * HP["n_layer"] + 1 if world > 1 else 0)
         line = {
             "metric": METRIC, "value": 1e3 / ms_per_step, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",

@@ -100,6 +100,16 @@ SIGNATURES: dict[str, tuple] = {
     "b200_copy_async": (c_int, [c_vp, c_u64, c_u64, c_u64]),
     "b200_repack_q4_0": (c_int, [c_vp, c_u64, c_int, c_int, c_u64]),
     "b200_device_count": (c_int, []),
+    # b200_comm.h
+    "b200_comm_create": (c_int, [P(c_vp), c_int, c_int, c_int, c_int]),
+    "b200_comm_handle_bytes": (c_int, []),
+    "b200_comm_export": (c_int, [c_vp, c_vp]),
+    "b200_comm_import": (c_int, [c_vp, c_vp]),
+    "b200_allreduce_sum": (c_int, [c_vp, c_u64, c_int, c_vp]),
+    "b200_allgather": (c_int, [c_vp, c_u64, c_u64, c_int, c_vp]),
+    "b200_allgather_pick": (c_int, [c_vp, c_u64, c_u64, c_vp]),
+    "b200_comm_status": (c_int, [c_vp, P(c_uint)]),
+    "b200_comm_destroy": (c_int, [c_vp]),
     "b200_last_error": (c_char_p, []),
 }
 
