@@ -395,6 +395,52 @@ def kernel_roofline(torch, chain, reps: int) -> dict:
     return {"bytes_per_launch": total_bytes / launches, "s_per_launch": dur / launches, "launches": launches}
 
 
+def config2_shapes(world: int) -> list[tuple[str, int, int]]:
+    """every GEMV of one Llama-3.2-1B layer plus lm_head, as
+    one rank of `world` holds it (row split wq/wk/wv/w1/w3/lm_head, K split
+    wo/w2; tp_llama.cpp:238-247)."""
+    e, f, kv = HP["n_embd"], HP["n_ff"], HP["n_head_kv"] * HP["head_dim"]
+    return [("wq", e // world, e), ("wk", kv // world, e), ("wv", kv // world, e), ("wo", e, e // world),
+            ("w1", f // world, e), ("w3", f // world, e), ("w2", e, f // world), ("lm_head", HP["n_vocab"] // world, e)]
+
+
+def per_gemv_table(pkg, torch, eng, stream, world: int, device: int, launches: int = 200) -> dict:
+    """Achieved GB/s of each config-2 GEMV run back to back as independent
+    calls: `copies` copies of the matrix (together > 2 x L2) used round robin,
+    so every launch streams its weights from HBM; device time per launch from
+    CUDA events on the engine's stream over `launches` calls after a warm-up
+    round."""
+    peak, _ = hbm_peak()
+    out = {}
+    dev = f"cuda:{device}"
+    x = torch.randn(HP["n_ff"], dtype=torch.float32, device=dev)
+    for name, rows, k in config2_shapes(world):
+        one = pkg.tiled_bytes(rows, k)
+        copies = max(2, -(-2 * L2_BYTES // one))
+        raw = synth_q4_0(rows, k, WEIGHT_SEED + 77)
+        W0 = eng.repack(pkg.QMat(torch.from_numpy(raw.reshape(-1)).to(dev), rows, k))
+        buf = torch.empty(copies * one, dtype=torch.uint8, device=dev)
+        for c in range(copies):
+            buf[c * one:(c + 1) * one].copy_(W0.blocks[:one])
+        mats = [pkg.QMat(buf[c * one:(c + 1) * one], rows, k, pkg.LAYOUT_TILES) for c in range(copies)]
+        y = torch.empty(rows, dtype=torch.float32, device=dev)
+        torch.cuda.synchronize(device)
+        for W in mats[:min(copies, 8)]:
+            eng.gemv_f32(W, x[:k], y)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for i in range(launches):
+            eng.gemv_f32(mats[i % copies], x[:k], y)
+        b.record(stream)
+        b.synchronize()
+        us = a.elapsed_time(b) * 1e3 / launches
+        gbs = algorithmic_bytes(rows, k) / us / 1e3
+        out[name] = {"rows": rows, "k": k, "us": round(us, 3), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+        del mats, buf, W0, y
+    return out
+
+
 def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     import torch
     import __graft_entry__
@@ -446,9 +492,18 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     barrier(world)
     ms_e2e = max_over_ranks(ms_e2e, world)
 
-    roof = kernel_roofline(torch, chain, reps=3)
     peak, peak_kind = hbm_peak()
-    achieved = roof["bytes_per_launch"] / roof["s_per_launch"] / 1e9
+    # Roofline of the GEMV kernel inside the timed region: the token graph runs
+    # its 65 GEMV launches back to back, each waiting on its predecessor, so the
+    # average launch duration is the step time over 65 (at N = 1 every kernel of
+    # the step is this GEMV; at N > 1 the step also holds the exchange kernels,
+    # so the figure is a lower bound on the GEMV's own rate).
+    n_gemv = len(chain.mats)
+    gemv_bytes = chain.gemv_bytes()
+    per_launch_s = ms_per_step * 1e-3 / n_gemv
+    achieved = gemv_bytes / n_gemv / per_launch_s / 1e9
+    iso = kernel_roofline(torch, chain, reps=3)
+    per_gemv = per_gemv_table(pkg, torch, chain.eng, chain.stream, world, local_rank) if args.per_gemv else None
 
     line = None
     if rank == 0:
@@ -475,8 +530,12 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                               else "per-rank weights larger than L2, no flush")},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
-                         "kernel": "q4_tile_kernel (Q4_0 x Q8_0 GEMV, tile layout)",
-                         "per_launch_bytes": roof["bytes_per_launch"], "per_launch_us": roof["s_per_launch"] * 1e6},
+                         "kernel": "q4_tile_kernel (Q4_0 x Q8_0 GEMV, fused Q8_0 quantise, tile layout)",
+                         "per_launch_bytes": gemv_bytes / n_gemv, "per_launch_us": per_launch_s * 1e6,
+                         "method": "step time / 65 GEMV launches of the token graph (CUDA events, engine stream)"
+                                   + ("" if world == 1 else "; step includes the exchange kernels"),
+                         "eager_isolated_per_launch_us": iso["s_per_launch"] * 1e6},
+            "per_gemv": per_gemv,
             "cpu_baseline": cpu,
             "e2e": {"value": 1e3 * args.steps / ms_e2e, "unit": UNIT, "h2d_bytes_per_step": chain.x0.numel() * 4,
                     "d2h_bytes_per_step": 8},
@@ -512,6 +571,8 @@ def main() -> None:
     ap.add_argument("--ctas-per-sm", dest="ctas_per_sm", type=int, default=4)
     ap.add_argument("--fuse-quantize", dest="fuse_quantize", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--no-per-gemv", dest="per_gemv", action="store_false",
+                    help="skip the per-GEMV table of config 2's shapes")
     args = ap.parse_args()
     rank, world, local_rank = dist_env()
     if world != args.gpus:

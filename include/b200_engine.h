@@ -4,9 +4,11 @@
  * makes per matrix: quantise float32 x to Q8_0, run the Q4_0 GEMV, and name
  * the matrix that comes next so its bytes can start moving early.
  *
- * Weights stay in the GGUF Q4_0 row layout (18-byte blocks, row-major), one
- * contiguous 16-byte-aligned allocation per matrix; no repack. Results are
- * bit-exact to src/llm_kv260/q4_0.py:185-188 (gemv_q4_0_f32).
+ * Weights are one contiguous 16-byte-aligned allocation per matrix, either
+ * in the GGUF Q4_0 row layout (18-byte blocks, row-major) or re-laid once at
+ * load into the engine's tiles (b200_repack_q4_0), which the fast kernel
+ * reads. Results are bit-exact to src/llm_kv260/q4_0.py:185-188
+ * (gemv_q4_0_f32).
  *
  * All addresses are CUDA device addresses; all functions return 0 or a
  * negative errno value (see gemv_dev.h), and b200_last_error() says why.
