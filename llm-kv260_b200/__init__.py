@@ -1,6 +1,7 @@
 """llm-kv260 on B200: the Q4_0 x Q8_0 GEMV and the rank-ordered fp32
 all-reduce of al-nafisah/llm-kv260's decode hot path, as sm_100a kernels
-behind a C ABI (include/*.h) shaped like the reference's board/kv260gemv.
+behind a C ABI (include/*.h) shaped like the reference's board/kv260gemv,
+and the greedy decoder built on them (Decoder, include/b200_decoder.h).
 
 The directory name has a hyphen, so it is loaded by path as module
 ``llm_kv260_b200`` (``__graft_entry__.load_package()``).
@@ -8,9 +9,10 @@ The directory name has a hyphen, so it is loaded by path as module
 
 from __future__ import annotations
 
-from . import capi
+from . import capi, model
 from .capi import B200Error, lib
+from .decoder import Decoder
 from .engine import LAYOUT_ROWS, LAYOUT_TILES, Engine, Gemv2Dev, GemvDev, QMat, Udmabuf, dev_ptr, tiled_bytes
 
-__all__ = ["B200Error", "Engine", "Gemv2Dev", "GemvDev", "LAYOUT_ROWS", "LAYOUT_TILES", "QMat", "Udmabuf", "capi",
-           "dev_ptr", "lib", "tiled_bytes"]
+__all__ = ["B200Error", "Decoder", "Engine", "Gemv2Dev", "GemvDev", "LAYOUT_ROWS", "LAYOUT_TILES", "QMat", "Udmabuf", "capi",
+           "dev_ptr", "lib", "model", "tiled_bytes"]

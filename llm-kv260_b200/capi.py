@@ -47,6 +47,13 @@ class b200_engine_config_t(ctypes.Structure):
 
 
 P = ctypes.POINTER
+class b200_decoder_config_t(ctypes.Structure):
+    """include/b200_decoder.h"""
+    _fields_ = [(n, c_int) for n in ("n_layer", "n_embd", "n_ff", "n_head", "n_head_kv", "head_dim", "n_vocab")] + \
+               [("rope_base", ctypes.c_float), ("rms_eps", ctypes.c_float)] + \
+               [(n, c_int) for n in ("ctx_max", "kv_f16", "round_mode", "exact_norm")]
+
+
 SIGNATURES: dict[str, tuple] = {
     # gemv_dev.h
     "gemv_dev_open": (c_int, [P(gemv_dev_t)]),
@@ -110,6 +117,17 @@ SIGNATURES: dict[str, tuple] = {
     "b200_allgather_pick": (c_int, [c_vp, c_u64, c_u64, c_vp]),
     "b200_comm_status": (c_int, [c_vp, P(c_uint)]),
     "b200_comm_destroy": (c_int, [c_vp]),
+    # b200_decoder.h
+    "b200_decoder_create": (c_int, [P(c_vp), P(b200_decoder_config_t), c_int, c_int, c_int, c_vp]),
+    "b200_decoder_set_layer": (c_int, [c_vp, c_int] + [c_vp] * 9),
+    "b200_decoder_set_output": (c_int, [c_vp, c_vp, c_vp]),
+    "b200_decoder_forward": (c_int, [c_vp, c_int, c_int, P(ctypes.c_int32), P(ctypes.c_float)]),
+    "b200_decoder_generate": (c_int, [c_vp, c_vp, c_int, c_int, c_vp, P(ctypes.c_double), P(ctypes.c_double)]),
+    "b200_decoder_read": (c_int, [c_vp, c_int, c_vp, c_u64]),
+    "b200_decoder_status": (c_int, [c_vp, P(c_uint)]),
+    "b200_rope_table": (c_int, [c_vp, c_int, c_int, ctypes.c_float]),
+    "b200_decoder_stream": (c_vp, [c_vp]),
+    "b200_decoder_destroy": (c_int, [c_vp]),
     "b200_last_error": (c_char_p, []),
 }
 

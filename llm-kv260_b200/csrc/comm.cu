@@ -38,6 +38,7 @@
 
 #include "../../include/b200_comm.h"
 #include "common.cuh"
+#include "decode.h"
 
 namespace b200 {
 
@@ -386,3 +387,19 @@ extern "C" int b200_comm_destroy(b200_comm_t *c) {
     free(c);
     return 0;
 }
+
+namespace b200 {
+
+int comm_word_area(b200_comm_t *c, uint64_t *win_words[kMaxDecodeRanks], uint64_t *slot_words, unsigned **status,
+                   int *rank, int *nranks) {
+    if (!c || (c->nranks > 1 && !c->imported)) return kErrInval;
+    for (int r = 0; r < kMaxDecodeRanks; ++r)
+        win_words[r] = r < c->nranks ? reinterpret_cast<uint64_t *>(c->params.win[r]) : nullptr;
+    *slot_words = c->params.slot_words;
+    *status = reinterpret_cast<unsigned *>(c->win + c->params.off_status);
+    *rank = c->rank;
+    *nranks = c->nranks;
+    return 0;
+}
+
+}  // namespace b200

@@ -82,6 +82,53 @@ int prefetch_l2_launch(const uint8_t *const *region, int nregions, size_t bytes_
 constexpr int kTileRows = 16;
 constexpr int kTileBytes = kTileRows * kLanes * kBlockBytes;  // 2304
 
+// ----------------------------------------------------------- decoder ops
+// What the decoder (decoder.cu) fuses into a tile GEMV, around the block dots.
+//
+// Prologue: how the CTA makes its float32 x before quantising it.
+enum Prologue : int {
+    kProPlain = 0,      // x as given
+    kProRmsnorm = 1,    // x = rmsnorm(res) * norm_w (tp_llama.cpp:557-569)
+    kProEmbedNorm = 2,  // res = embed(tokens[*pos]) (tp_llama.cpp:593-604, CTA 0 writes it), then as kProRmsnorm
+};
+// Epilogue: what happens to each finished row value v.
+enum Epilogue : int {
+    kEpiStore = 0,      // y[row] = v
+    kEpiRopeKv = 1,     // q|k|v rows: rope q and k (tp_llama.cpp:581-591), q, k, v -> y, k and v -> the KV cache at *pos
+    kEpiSiluPairs = 2,  // rows interleaved gate0, up0, gate1, ...: act[row / 2] = silu(gate) * up (tp_llama.cpp:615-622)
+    kEpiResidual = 3,   // res[row] += v with one rank; with several, += the rank-ordered sum of every rank's v
+                        // for that row (tp_llama.cpp:515-521 then add_into), exchanged through peer windows
+};
+
+constexpr int kMaxDecodeRanks = 8;
+
+struct DecodeOps {
+    int pro = kProPlain;
+    int epi = kEpiStore;
+    float *res = nullptr;              // residual stream x (kProRmsnorm/kProEmbedNorm: [k]; kEpiResidual: [rows])
+    const float *norm_w = nullptr;     // RMSNorm weight [k]
+    float eps = 0.0f;
+    int exact_norm = 0;                // 1: always sum the squares in the reference's order
+    const uint8_t *embd = nullptr;     // token_embd, GGUF Q4_0 rows [n_vocab][k/32*18]
+    const int *tokens = nullptr;       // token id by position
+    const int *pos = nullptr;          // the current position (device)
+    const float *rope_cs = nullptr;    // [ctx_max][head_dim]: cos, sin of pair i at 2i, 2i+1
+    int head_dim = 0, q_rows = 0, kv_rows = 0, ctx_max = 0, kv_f16 = 1;
+    void *kcache = nullptr;            // this layer's caches, [kv head][ctx_max][head_dim]
+    void *vcache = nullptr;
+    float *act = nullptr;              // kEpiSiluPairs output [rows / 2]
+    int nranks = 1, rank = 0;          // kEpiResidual across ranks:
+    uint64_t *win_words[kMaxDecodeRanks] = {};  // every rank's word area as mapped here, [slot][source rank][row]
+    uint64_t slot_words = 0;           // words per (slot, source rank)
+    const unsigned *step = nullptr;    // tokens done; epoch = step * ar_per_token + ar_index + 1
+    int ar_per_token = 0, ar_index = 0;
+    unsigned *peer_status = nullptr;   // bit kStatusPeerTimeout on a wait that ran out
+    int *adv_pos = nullptr;            // with a fused pick: after it, the token loop advances (one rank)
+    unsigned *adv_step = nullptr;
+    int *adv_tokens = nullptr;         // tokens[pos + 1] = the pick when pos + 1 >= *n_prompt
+    const int *n_prompt = nullptr;
+};
+
 struct TileLaunch {
     const uint8_t *w = nullptr;  // tiles
     int rows = 0;
@@ -96,6 +143,7 @@ struct TileLaunch {
     int *sel_out = nullptr;       // 8 bytes: int32 index + sel_base, float32 value
     int sel_base = 0;
     void *sel_scratch = nullptr;  // tile_select_scratch_bytes(), ticket zeroed once
+    DecodeOps dec;                // decoder prologue/epilogue (plain GEMV by default)
 };
 int tile_select_scratch_bytes();
 

@@ -29,6 +29,7 @@
 #include <cuda_fp16.h>
 
 #include "common.cuh"
+#include "decode.cuh"
 
 namespace b200 {
 
@@ -62,7 +63,123 @@ struct TileParams {
     int sel_base;
     float2 *sel_cand;    // gridDim.x entries: (value, row as float bits)
     unsigned *sel_ticket;
+    DecodeOps dec;       // decoder prologue / epilogue (q4gemv.h)
 };
+
+constexpr uint64_t kPeerTimeoutNs = 1000000000ull;  // a peer's row words: 1 s
+
+__device__ __forceinline__ void st_word(uint64_t *p, uint64_t w) {
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_word(const uint64_t *p) {
+    uint64_t w;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+// Decoder prologue: x = rmsnorm(res) * norm_w, quantised into xs (the same
+// layout as stage_x). One thread per 32-block. res is the residual stream,
+// or (kProEmbedNorm) the token's embedding row, which CTA 0 also writes to
+// res. The sum of squares runs in parallel in double; rms_float_is_safe
+// decides whether its float is the reference's, else threads 0-3 redo the
+// four lane sums in the reference's order from the copy of x in xf.
+__device__ __noinline__ void stage_x_norm(const TileParams &p, uint8_t *xs, float *xf, double *dred) {
+    __shared__ float s_f;
+    __shared__ int s_exact;
+    const int k = p.k, nb = k / kQK, b = threadIdx.x, lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+    float v[32];
+    double ss = 0.0;
+    if (b < nb) {
+        if (p.dec.pro == kProEmbedNorm) {
+            const int tok = p.dec.tokens[*p.dec.pos];
+            const uint16_t *blk =
+                reinterpret_cast<const uint16_t *>(p.dec.embd + (static_cast<size_t>(tok) * nb + b) * kBlockBytes);
+            uint16_t h[9];
+#pragma unroll
+            for (int j = 0; j < 9; ++j) h[j] = blk[j];
+            const float d = __half2float(__ushort_as_half(h[0]));
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int byte = (h[1 + j / 2] >> (8 * (j & 1))) & 0xff;
+                v[j] = __fmul_rn(__int2float_rn((byte & 0xF) - 8), d);
+                v[j + 16] = __fmul_rn(__int2float_rn((byte >> 4) - 8), d);
+            }
+            if (blockIdx.x == 0) {
+                float4 *dst = reinterpret_cast<float4 *>(p.dec.res) + 8 * b;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            }
+        } else {
+            const float4 *src = reinterpret_cast<const float4 *>(p.dec.res) + 8 * b;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float4 f = src[j];
+                v[4 * j] = f.x;
+                v[4 * j + 1] = f.y;
+                v[4 * j + 2] = f.z;
+                v[4 * j + 3] = f.w;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ss = __dadd_rn(ss, __dmul_rn(static_cast<double>(v[j]), static_cast<double>(v[j])));
+        float4 *xd = reinterpret_cast<float4 *>(xf) + 8 * b;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) xd[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(kFullMask, ss, off));
+    if (lane == 0) dred[warp] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double tot = 0.0;
+        for (int w = 0; w < static_cast<int>(blockDim.x / 32); ++w) tot = __dadd_rn(tot, dred[w]);
+        const double q = __ddiv_rn(tot, static_cast<double>(k));
+        const float f = __double2float_rn(q);
+        s_exact = p.dec.exact_norm || !rms_float_is_safe(q, f, k);
+        s_f = f;
+    }
+    __syncthreads();
+    if (s_exact) {
+        // tp_llama.cpp:560-564: lane j sums x[i]^2 for i = j, j+4, ... in order
+        if (threadIdx.x < 4) {
+            double a = 0.0;
+            for (int i = threadIdx.x; i < k; i += 4)
+                a = __dadd_rn(a, __dmul_rn(static_cast<double>(xf[i]), static_cast<double>(xf[i])));
+            dred[threadIdx.x] = a;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const double ss2 = __dadd_rn(__dadd_rn(dred[0], dred[2]), __dadd_rn(dred[1], dred[3]));
+            s_f = __double2float_rn(__ddiv_rn(ss2, static_cast<double>(k)));
+        }
+        __syncthreads();
+    }
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s_f, p.dec.eps)));
+    if (b < nb) {
+        const float4 *wv = reinterpret_cast<const float4 *>(p.dec.norm_w) + 8 * b;
+        float4 hv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float4 w4 = __ldg(wv + j);
+            hv[j].x = __fmul_rn(__fmul_rn(v[4 * j], scale), w4.x);
+            hv[j].y = __fmul_rn(__fmul_rn(v[4 * j + 1], scale), w4.y);
+            hv[j].z = __fmul_rn(__fmul_rn(v[4 * j + 2], scale), w4.z);
+            hv[j].w = __fmul_rn(__fmul_rn(v[4 * j + 3], scale), w4.w);
+        }
+        uint32_t q[8];
+        float d;
+        const int sum = q8_quant_block(hv, p.round_mode, q, &d);
+        uint4 *qdst = reinterpret_cast<uint4 *>(xs + 32 * b);
+        qdst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+        qdst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+        reinterpret_cast<int2 *>(xs + k)[b] = make_int2(__float_as_int(__half2float(__float2half_rn(d))), sum);
+    }
+}
+
+// Byte offset of the decoder's x copy (xf) after the staged x, and its size.
+__host__ __device__ constexpr int xarea_bytes(int k) { return (k + 8 * (k / kQK) + 15) / 16 * 16; }
+constexpr int norm_extra_bytes(int k) { return 4 * k + 32 * 8; }  // xf [k] floats + 32 doubles
 
 // (value desc, index asc); NaN never beats a number (the scan's rule for any
 // index but 0, which the final step handles).
@@ -123,8 +240,21 @@ __global__ void __launch_bounds__(kTileThreads * KS) q4_tile_kernel(const __grid
     pdl_wait_prior_grid();
 
     // One thread per x block: 128*KS threads >= 8*nch blocks, as KS >= nch/8.
-    stage_x<XMODE>(p.x, p.k, p.round_mode, xs);
+    if (XMODE == kXF32 && p.dec.pro != kProPlain)
+        stage_x_norm(p, xs, reinterpret_cast<float *>(xs + xarea_bytes(p.k)),
+                     reinterpret_cast<double *>(xs + xarea_bytes(p.k) + 4 * p.k));
+    else
+        stage_x<XMODE>(p.x, p.k, p.round_mode, xs);
     __syncthreads();
+    const int epi = p.dec.epi;
+    const int dpos = (epi == kEpiRopeKv) ? *p.dec.pos : 0;
+    const bool xchg = epi == kEpiResidual && p.dec.nranks > 1;
+    uint32_t epoch = 0;
+    uint64_t slot_off = 0;
+    if (xchg) {
+        epoch = *p.dec.step * static_cast<uint32_t>(p.dec.ar_per_token) + static_cast<uint32_t>(p.dec.ar_index) + 1u;
+        slot_off = static_cast<uint64_t>(epoch & 1u) * kMaxDecodeRanks * p.dec.slot_words;
+    }
     const int c_first = slice * CPS;
     XBlock xr[CPS];
 #pragma unroll
@@ -167,13 +297,88 @@ __global__ void __launch_bounds__(kTileThreads * KS) q4_tile_kernel(const __grid
             const float yv = tree8(r[0 * kTileRows], r[1 * kTileRows], r[2 * kTileRows], r[3 * kTileRows],
                                    r[4 * kTileRows], r[5 * kTileRows], r[6 * kTileRows], r[7 * kTileRows]);
             const int row = (g0 + s) * kTileRows + t;
-            if (row < p.rows) {
-                p.y[row] = yv;
-                if (sel_better(yv, row, best_v, best_i)) {
-                    best_v = yv;
-                    best_i = row;
+            const bool live = row < p.rows;
+            if (epi == kEpiStore) {
+                if (live) {
+                    p.y[row] = yv;
+                    if (sel_better(yv, row, best_v, best_i)) {
+                        best_v = yv;
+                        best_i = row;
+                    }
+                }
+            } else if (epi == kEpiRopeKv) {
+                // q and k rows start at multiples of head_dim (even), and a row
+                // group at a multiple of 16, so rope's pair (2i, 2i+1) is this
+                // thread and its neighbour t ^ 1
+                const float other = __shfl_xor_sync(0x0000ffffu, yv, 1);
+                if (live) {
+                    const int hd = p.dec.head_dim, k0 = p.dec.q_rows, v0 = k0 + p.dec.kv_rows;
+                    float out = yv;
+                    if (row < v0) {
+                        const int i = (row % hd) >> 1;
+                        const float *cs = p.dec.rope_cs + static_cast<size_t>(dpos) * hd;
+                        const bool even = !(row & 1);
+                        out = rope_pair(even ? yv : other, even ? other : yv, cs[2 * i], cs[2 * i + 1], even);
+                    }
+                    p.y[row] = out;
+                    if (row >= k0) {
+                        const bool isk = row < v0;
+                        const int rr = row - (isk ? k0 : v0);
+                        const size_t at = (static_cast<size_t>(rr / hd) * p.dec.ctx_max + dpos) * hd + rr % hd;
+                        void *cache = isk ? p.dec.kcache : p.dec.vcache;
+                        if (p.dec.kv_f16)
+                            static_cast<__half *>(cache)[at] = __float2half_rn(out);
+                        else
+                            static_cast<float *>(cache)[at] = out;
+                    }
+                }
+            } else if (epi == kEpiSiluPairs) {
+                const float other = __shfl_xor_sync(0x0000ffffu, yv, 1);
+                if (live) {
+                    if (p.y) p.y[row] = yv;
+                    if (!(row & 1)) p.dec.act[row >> 1] = silu_mul(yv, other);
+                }
+            } else if (live) {  // kEpiResidual
+                if (p.y) p.y[row] = yv;
+                if (!xchg) {
+                    p.dec.res[row] = __fadd_rn(p.dec.res[row], yv);
+                } else {
+                    const uint64_t word = (static_cast<uint64_t>(epoch) << 32) | __float_as_uint(yv);
+                    const uint64_t at = slot_off + static_cast<uint64_t>(p.dec.rank) * p.dec.slot_words + row;
+                    for (int r = 0; r < p.dec.nranks; ++r) st_word(p.dec.win_words[r] + at, word);
                 }
             }
+        }
+    }
+    if (xchg && t < kTileRows && !s_abort) {
+        // Every rank computed these rows' partials for its K slice; collect
+        // them from this rank's window and sum in rank order
+        // (tp_llama.cpp:515-521), then add into the residual (add_into).
+        const uint64_t *own = p.dec.win_words[p.dec.rank] + slot_off;
+        for (int s2 = 0; s2 < nst; ++s2) {
+            const int row = (g0 + s2) * kTileRows + t;
+            if (row >= p.rows) continue;
+            float val[kMaxDecodeRanks];
+            unsigned pending = (1u << p.dec.nranks) - 1u;
+            const uint64_t t0 = globaltimer_ns();
+            for (unsigned spins = 0; pending; ++spins) {
+                for (int r = 0; r < p.dec.nranks; ++r) {
+                    if (!(pending & (1u << r))) continue;
+                    const uint64_t w = ld_word(own + static_cast<uint64_t>(r) * p.dec.slot_words + row);
+                    if (static_cast<uint32_t>(w >> 32) == epoch) {
+                        val[r] = __uint_as_float(static_cast<uint32_t>(w));
+                        pending &= ~(1u << r);
+                    }
+                }
+                if (pending && (spins & 63u) == 63u && globaltimer_ns() - t0 > kPeerTimeoutNs) {
+                    atomicOr(p.dec.peer_status, kStatusPeerTimeout);
+                    break;
+                }
+            }
+            if (pending) break;
+            float sum = val[0];
+            for (int r = 1; r < p.dec.nranks; ++r) sum = __fadd_rn(sum, val[r]);
+            p.dec.res[row] = __fadd_rn(p.dec.res[row], sum);
         }
     }
     if (p.sel_out) {
@@ -224,6 +429,14 @@ __global__ void __launch_bounds__(kTileThreads * KS) q4_tile_kernel(const __grid
                 p.sel_out[0] = bi + p.sel_base;
                 p.sel_out[1] = __float_as_int(bv);
                 *p.sel_ticket = 0;
+                if (p.dec.adv_pos) {
+                    // the decode loop's step (tp_llama.cpp:951-959): the pick is
+                    // the next position's token unless the prompt supplies it
+                    const int nx = *p.dec.adv_pos + 1;
+                    if (nx >= *p.dec.n_prompt && nx <= p.dec.ctx_max) p.dec.adv_tokens[nx] = bi + p.sel_base;
+                    *p.dec.adv_pos = nx;
+                    *p.dec.adv_step += 1u;
+                }
             }
         }
     }
@@ -327,8 +540,10 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
         p.sel_cand = static_cast<float2 *>(L.sel_scratch);
         p.sel_ticket = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(L.sel_scratch) + kSelMaxCtas * sizeof(float2));
     }
+    p.dec = L.dec;
     const int threads = kTileThreads * ks;
-    const int xarea = round_up(L.k + 8 * nb, 16);
+    if (L.dec.pro != kProPlain && nb > threads) return kErrInval;  // one thread per x block
+    const int xarea = xarea_bytes(L.k) + (L.dec.pro != kProPlain ? norm_extra_bytes(L.k) : 0);
     const int fixed = kSmemAlign + kBarBytes + kRedBytes + (ks > 1 ? nch * kTileThreads * 4 : 0) + xarea;
     const int limit = max_smem_optin();
     while (p.stages > 1 && fixed + p.stages * p.slot_bytes > limit) p.stages -= 1;
@@ -368,7 +583,38 @@ int tile_validate(const TileLaunch &L, const char **why) {
     if (L.rows <= 0) return bad("rows must be positive");
     if (!L.w || reinterpret_cast<uintptr_t>(L.w) % 16) return bad("tiles must be 16-byte aligned");
     if (!L.x || reinterpret_cast<uintptr_t>(L.x) % 16) return bad("x must be 16-byte aligned");
-    if (!L.y || reinterpret_cast<uintptr_t>(L.y) % 4) return bad("y must be 4-byte aligned");
+    const DecodeOps &D = L.dec;
+    const bool y_needed = D.epi == kEpiStore || D.epi == kEpiRopeKv;
+    if (y_needed ? (!L.y || reinterpret_cast<uintptr_t>(L.y) % 4) : (L.y && reinterpret_cast<uintptr_t>(L.y) % 4))
+        return bad("y must be 4-byte aligned");
+    if (D.pro < kProPlain || D.pro > kProEmbedNorm || D.epi < kEpiStore || D.epi > kEpiResidual)
+        return bad("unknown decoder prologue or epilogue");
+    if (D.pro != kProPlain) {
+        if (L.xmode != kXF32) return bad("a normalising prologue needs float32 x");
+        if (!D.res || !D.norm_w || reinterpret_cast<uintptr_t>(D.res) % 16 || reinterpret_cast<uintptr_t>(D.norm_w) % 16)
+            return bad("rmsnorm prologue: res and norm_w must be 16-byte aligned");
+        if (D.pro == kProEmbedNorm && (!D.embd || !D.tokens || !D.pos || reinterpret_cast<uintptr_t>(D.embd) % 2))
+            return bad("embedding prologue: token_embd, tokens and pos needed");
+    }
+    if (D.epi == kEpiRopeKv) {
+        if (!D.rope_cs || !D.kcache || !D.vcache || !D.pos || D.head_dim <= 0 || D.head_dim % 2 || D.q_rows % D.head_dim ||
+            D.kv_rows % D.head_dim || D.q_rows % kTileRows || D.kv_rows % kTileRows || D.ctx_max <= 0 ||
+            L.rows != D.q_rows + 2 * D.kv_rows)
+            return bad("rope/KV epilogue: inconsistent q/k/v rows, head_dim or caches");
+    }
+    if (D.epi == kEpiSiluPairs && (!D.act || L.rows % 2)) return bad("silu epilogue: act needed, rows even");
+    if (D.epi == kEpiResidual) {
+        if (!D.res) return bad("residual epilogue: res needed");
+        if (D.nranks < 1 || D.nranks > kMaxDecodeRanks || D.rank < 0 || D.rank >= D.nranks)
+            return bad("residual epilogue: bad rank count");
+        if (D.nranks > 1) {
+            if (!D.step || !D.peer_status || D.slot_words < static_cast<uint64_t>(L.rows)) return bad("residual exchange: window too small");
+            for (int r = 0; r < D.nranks; ++r)
+                if (!D.win_words[r]) return bad("residual exchange: a peer window is not mapped");
+        }
+    }
+    if (D.adv_pos && (!L.sel_out || !D.adv_step || !D.adv_tokens || !D.n_prompt))
+        return bad("advance needs the fused pick, step, tokens and n_prompt");
     return 0;
 }
 

@@ -1,0 +1,98 @@
+"""Python face of the greedy decoder (include/b200_decoder.h): the reference
+runtime's decode loop (board/tp/tp_llama.cpp:783-968) on B200."""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import capi
+from .capi import check, lib
+
+
+def _p(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+class Decoder:
+    """One rank's decoder. `model` is a dict as model.synth_model returns (or a
+    GGUF loader would): hparams, "layers", "token_embd", "output_norm"."""
+
+    def __init__(self, model: dict, device: int = 0, rank: int = 0, nranks: int = 1, comm=None,
+                 ctx_max: int = 512, kv_f16: bool = True, round_mode: int = 0, exact_norm: bool = False):
+        c = capi.b200_decoder_config_t()
+        for n in ("n_layer", "n_embd", "n_ff", "n_head", "n_head_kv", "head_dim", "n_vocab"):
+            setattr(c, n, int(model[n]))
+        c.rope_base, c.rms_eps = float(model["rope_base"]), float(model["rms_eps"])
+        c.ctx_max, c.kv_f16, c.round_mode, c.exact_norm = ctx_max, int(kv_f16), round_mode, int(exact_norm)
+        self.cfg, self.rank, self.nranks, self.ctx_max = c, rank, nranks, ctx_max
+        self.h = ctypes.c_void_p()
+        check(lib().b200_decoder_create(ctypes.byref(self.h), ctypes.byref(c), device, rank, nranks,
+                                        comm.h if comm is not None else None), "b200_decoder_create")
+        for i, L in enumerate(model["layers"]):
+            arrs = [np.ascontiguousarray(L[n]) for n in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate",
+                                                        "ffn_up", "ffn_down")]
+            norms = [np.ascontiguousarray(L[n], dtype=np.float32) for n in ("attn_norm", "ffn_norm")]
+            check(lib().b200_decoder_set_layer(self.h, i, *[_p(a) for a in arrs], *[_p(a) for a in norms]),
+                  "b200_decoder_set_layer")
+        te = np.ascontiguousarray(model["token_embd"])
+        on = np.ascontiguousarray(model["output_norm"], dtype=np.float32)
+        check(lib().b200_decoder_set_output(self.h, _p(te), _p(on)), "b200_decoder_set_output")
+
+    def forward(self, token: int, pos: int) -> tuple[int, float]:
+        """runtime::forward + the greedy pick over all ranks."""
+        t, v = ctypes.c_int32(0), ctypes.c_float(0.0)
+        check(lib().b200_decoder_forward(self.h, token, pos, ctypes.byref(t), ctypes.byref(v)), "b200_decoder_forward")
+        return int(t.value), float(v.value)
+
+    def generate(self, prompt, n_gen: int) -> tuple[np.ndarray, float, float]:
+        """Greedy generate: (tokens, prompt_ms, gen_ms) -- device time of the
+        prompt's forwards and of the remaining n_gen - 1."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.empty(n_gen, dtype=np.int32)
+        pm, gm = ctypes.c_double(0.0), ctypes.c_double(0.0)
+        check(lib().b200_decoder_generate(self.h, _p(p), p.shape[0], n_gen, _p(out), ctypes.byref(pm),
+                                          ctypes.byref(gm)), "b200_decoder_generate")
+        return out, pm.value, gm.value
+
+    def _read(self, what: int, n: int, dtype) -> np.ndarray:
+        out = np.empty(n, dtype=dtype)
+        check(lib().b200_decoder_read(self.h, what, _p(out), out.nbytes), "b200_decoder_read")
+        return out
+
+    def residual(self) -> np.ndarray:
+        return self._read(0, self.cfg.n_embd, np.float32)
+
+    def logits(self) -> np.ndarray:
+        return self._read(1, self.cfg.n_vocab // self.nranks, np.float32)
+
+    def tokens(self) -> np.ndarray:
+        return self._read(2, self.ctx_max + 1, np.int32)
+
+    def status(self) -> int:
+        s = ctypes.c_uint(0)
+        check(lib().b200_decoder_status(self.h, ctypes.byref(s)), "b200_decoder_status")
+        return int(s.value)
+
+    @property
+    def stream(self) -> int:
+        return int(lib().b200_decoder_stream(self.h) or 0)
+
+    def close(self) -> None:
+        if self.h:
+            lib().b200_decoder_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def rope_table(d: int, pos: int, base: float) -> np.ndarray:
+    """The host RoPE table the decoder uploads (b200_rope_table)."""
+    cs = np.empty(d, dtype=np.float32)
+    check(lib().b200_rope_table(_p(cs), d, pos, base), "b200_rope_table")
+    return cs

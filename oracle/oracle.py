@@ -35,8 +35,9 @@ _lib = None
 
 def build(force: bool = False) -> str:
     """Compile the C restatement with its Makefile (gcc, -ffp-contract=off)."""
-    src = os.path.join(_HERE, "q4_0_oracle.c")
-    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+    srcs = [os.path.join(_HERE, f) for f in ("q4_0_oracle.c", "q4_0_oracle.h", "decode_oracle.c", "decode_oracle.h")]
+    newest = max(os.path.getmtime(f) for f in srcs)
+    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < newest:
         subprocess.run(["make", "-s", "-C", _HERE], check=True)
     return _LIB_PATH
 
@@ -62,6 +63,18 @@ def lib() -> ctypes.CDLL:
             "oracle_gemv_q4_0_packed": (I, [P, I64, I64, P, P, I]),
             "oracle_gemv2_chunk_offset": (I64, [I, I, I, I, ctypes.POINTER(ctypes.c_int)]),
             "oracle_allreduce_ordered": (I, [P, I, I64, P]),
+            "odec_v_expf": (ctypes.c_float, [ctypes.c_float]),
+            "odec_rmsnorm": (None, [P, P, P, I, ctypes.c_float]),
+            "odec_rope_table": (None, [P, I, I, ctypes.c_float]),
+            "odec_rope": (None, [P, I, I, P]),
+            "odec_silu_mul": (None, [P, P, P, I]),
+            "odec_embed": (None, [P, P, I, I]),
+            "odec_attention": (None, [I, P, P, P, I, I64, I, I, ctypes.c_float, P, I, P]),
+            "odec_create": (I, [P, P, P, P, P]),
+            "odec_destroy": (None, [P]),
+            "odec_forward": (I, [P, I, I, P, P]),
+            "odec_generate": (I, [P, P, I, I, P]),
+            "odec_read": (I, [P, I, I, P, I64]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -239,3 +252,146 @@ def allreduce_ordered(partials: list[np.ndarray]) -> np.ndarray:
     _check(lib().oracle_allreduce_ordered(ctypes.cast(ptrs, ctypes.c_void_p), n, length, _ptr(out)),
            "allreduce_ordered")
     return out
+
+
+# ------------------------------------------------------------------ decode step
+# decode_oracle.c: runtime::forward of board/tp/tp_llama.cpp (822-883) and its
+# ops, restated per NEON lane; parity with the reference itself is unpinned.
+
+def v_expf(x: float) -> float:
+    """tp_llama.cpp:530-553 (one lane)."""
+    return float(lib().odec_v_expf(float(x)))
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """tp_llama.cpp:557-569."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    if x.shape != w.shape or x.ndim != 1 or x.shape[0] % 4:
+        raise ValueError("x and w must be 1-D of one length, a multiple of 4")
+    out = np.empty_like(x)
+    lib().odec_rmsnorm(_ptr(out), _ptr(x), _ptr(w), x.shape[0], eps)
+    return out
+
+
+def rope_table(d: int, pos: int, base: float) -> np.ndarray:
+    """tp_llama.cpp:574-580 without freq factors: cos, sin interleaved, d floats."""
+    cs = np.empty(d, dtype=np.float32)
+    lib().odec_rope_table(_ptr(cs), d, pos, base)
+    return cs
+
+
+def rope(x: np.ndarray, n_heads: int, d: int, cs: np.ndarray) -> np.ndarray:
+    """tp_llama.cpp:581-591, on a copy."""
+    y = np.array(x, dtype=np.float32, copy=True)
+    cs = np.ascontiguousarray(cs, dtype=np.float32)
+    lib().odec_rope(_ptr(y), n_heads, d, _ptr(cs))
+    return y
+
+
+def silu_mul(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    """tp_llama.cpp:615-622."""
+    g = np.ascontiguousarray(gate, dtype=np.float32)
+    u = np.ascontiguousarray(up, dtype=np.float32)
+    out = np.empty_like(g)
+    lib().odec_silu_mul(_ptr(out), _ptr(g), _ptr(u), g.shape[0])
+    return out
+
+
+def embed(token_embd: np.ndarray, token: int, n_embd: int) -> np.ndarray:
+    """tp_llama.cpp:593-604."""
+    t = np.ascontiguousarray(token_embd, dtype=np.uint8)
+    out = np.empty(n_embd, dtype=np.float32)
+    lib().odec_embed(_ptr(out), _ptr(t), token, n_embd)
+    return out
+
+
+def attention(q: np.ndarray, kc: np.ndarray, vc: np.ndarray, pos: int, scale: float) -> np.ndarray:
+    """attention_group (tp_llama.cpp:644-690): q [B, d] float32; kc, vc
+    [>= pos+1, d] float32 or float16 (their bits used as stored)."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    B, d = q.shape
+    f16 = kc.dtype == np.float16
+    kc = np.ascontiguousarray(kc)
+    vc = np.ascontiguousarray(vc)
+    sc = np.empty((B, pos + 1), dtype=np.float32)
+    out = np.empty((B, d), dtype=np.float32)
+    lib().odec_attention(B, _ptr(q), _ptr(kc), _ptr(vc), int(f16), d, pos, d, scale, _ptr(sc), pos + 1, _ptr(out))
+    return out
+
+
+class _Config(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("n_layer", "n_embd", "n_ff", "n_head", "n_head_kv", "head_dim",
+                                            "n_vocab")] + \
+               [("rope_base", ctypes.c_float), ("rms_eps", ctypes.c_float)] + \
+               [(n, ctypes.c_int) for n in ("ctx_max", "kv_f16", "nranks", "round_mode", "threads")]
+
+
+class _Layer(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up",
+                                               "ffn_down", "attn_norm", "ffn_norm")]
+
+
+class Decoder:
+    """The reference runtime's decode loop on the CPU, nranks shards simulated.
+
+    `model` is a dict: hparams (n_layer, n_embd, n_ff, n_head, n_head_kv,
+    head_dim, n_vocab, rope_base, rms_eps), "layers" (a list of dicts with
+    attn_q, attn_k, attn_v, attn_output, ffn_gate, ffn_up, ffn_down as
+    uint8 GGUF Q4_0 rows and attn_norm, ffn_norm as float32), "token_embd"
+    and "output_norm"."""
+
+    def __init__(self, model: dict, nranks: int = 1, ctx_max: int = 512, kv_f16: bool = True,
+                 round_mode: int = ROUND_CONTRACT, threads: int | None = None):
+        c = _Config()
+        for n in ("n_layer", "n_embd", "n_ff", "n_head", "n_head_kv", "head_dim", "n_vocab"):
+            setattr(c, n, int(model[n]))
+        c.rope_base, c.rms_eps = float(model["rope_base"]), float(model["rms_eps"])
+        c.ctx_max, c.kv_f16, c.nranks, c.round_mode = ctx_max, int(kv_f16), nranks, round_mode
+        c.threads = threads or default_threads()
+        self.n_vocab, self.n_embd, self.nranks = c.n_vocab, c.n_embd, nranks
+        keep = []
+        layers = (_Layer * c.n_layer)()
+        for i, L in enumerate(model["layers"]):
+            for n in _Layer._fields_:
+                a = np.ascontiguousarray(L[n[0]])
+                keep.append(a)
+                setattr(layers[i], n[0], _ptr(a))
+        te = np.ascontiguousarray(model["token_embd"], dtype=np.uint8)
+        on = np.ascontiguousarray(model["output_norm"], dtype=np.float32)
+        self._h = ctypes.c_void_p()
+        _check(lib().odec_create(ctypes.byref(self._h), ctypes.byref(c), ctypes.cast(layers, ctypes.c_void_p),
+                                 _ptr(te), _ptr(on)), "odec_create")
+
+    def forward(self, token: int, pos: int) -> tuple[int, float]:
+        t, v = ctypes.c_int(0), ctypes.c_float(0.0)
+        _check(lib().odec_forward(self._h, token, pos, ctypes.byref(t), ctypes.byref(v)), "odec_forward")
+        return int(t.value), float(v.value)
+
+    def generate(self, prompt, n_gen: int) -> np.ndarray:
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.empty(n_gen, dtype=np.int32)
+        _check(lib().odec_generate(self._h, _ptr(p), p.shape[0], n_gen, _ptr(out)), "odec_generate")
+        return out
+
+    def residual(self) -> np.ndarray:
+        out = np.empty(self.n_embd, dtype=np.float32)
+        _check(lib().odec_read(self._h, 0, 0, _ptr(out), self.n_embd), "odec_read")
+        return out
+
+    def logits(self, rank: int = 0) -> np.ndarray:
+        n = self.n_vocab // self.nranks
+        out = np.empty(n, dtype=np.float32)
+        _check(lib().odec_read(self._h, 1, rank, _ptr(out), n), "odec_read")
+        return out
+
+    def close(self) -> None:
+        if self._h:
+            lib().odec_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,111 @@
+"""The B200 decoder against the decode-step oracle, bit for bit: after every
+forward the residual stream and this rank's logits must have the oracle's
+bits, and every greedy token must be the oracle's. Models are seeded
+random-init Q4_0 (llm-kv260_b200/model.py); the oracle runs on the host."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+HD64 = dict(n_layer=2, n_embd=512, n_ff=1024, n_head=8, n_head_kv=2, head_dim=64, n_vocab=1024,
+            rope_base=500000.0, rms_eps=1e-5)
+HD128 = dict(n_layer=2, n_embd=768, n_ff=1536, n_head=6, n_head_kv=2, head_dim=128, n_vocab=1024,
+             rope_base=500000.0, rms_eps=1e-5)
+
+
+def bits(a: np.ndarray) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+def step_by_step(pkg, oracle, hp, seed, n_prompt, n_steps, ctx_max=64, **kw):
+    from llm_kv260_b200 import model
+    m = model.synth_model(hp, seed=seed)
+    dec = pkg.Decoder(m, ctx_max=ctx_max, **kw)
+    ref = oracle.Decoder(m, nranks=1, ctx_max=ctx_max, kv_f16=kw.get("kv_f16", True),
+                         round_mode=kw.get("round_mode", 0))
+    prompt = model.random_prompt(n_prompt, hp["n_vocab"], seed=seed + 1)
+    tok = None
+    for i in range(n_steps):
+        inp = int(prompt[i]) if i < n_prompt else tok
+        tg, vg = dec.forward(inp, i)
+        tr, vr = ref.forward(inp, i)
+        assert np.array_equal(bits(dec.residual()), bits(ref.residual())), f"residual differs at position {i}"
+        assert np.array_equal(bits(dec.logits()), bits(ref.logits())), f"logits differ at position {i}"
+        assert (tg, np.float32(vg).view(np.uint32)) == (tr, np.float32(vr).view(np.uint32)), i
+        tok = tr
+    dec.close()
+    ref.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kw", [dict(), dict(kv_f16=False), dict(round_mode=1), dict(exact_norm=True)],
+                         ids=["f16kv", "f32kv", "roundf", "exact_norm"])
+def test_forward_bit_exact_hd64(cuda_lib, pkg, oracle, kw):
+    step_by_step(pkg, oracle, HD64, seed=21, n_prompt=5, n_steps=12, **kw)
+
+
+@pytest.mark.gpu
+def test_forward_bit_exact_hd128_group3(cuda_lib, pkg, oracle):
+    step_by_step(pkg, oracle, HD128, seed=22, n_prompt=4, n_steps=10)
+
+
+@pytest.mark.gpu
+def test_long_context_crosses_attention_chunks(cuda_lib, pkg, oracle):
+    """More positions than one 128-position V chunk, and a tail that is not a
+    multiple of 4 (softmax's scalar tail)."""
+    hp = dict(HD64, n_layer=1)
+    step_by_step(pkg, oracle, hp, seed=23, n_prompt=290, n_steps=291, ctx_max=300)
+
+
+@pytest.mark.gpu
+def test_generate_matches_oracle(cuda_lib, pkg, oracle):
+    from llm_kv260_b200 import model
+    m = model.synth_model(HD64, seed=24)
+    prompt = model.random_prompt(7, HD64["n_vocab"], seed=25)
+    dec = pkg.Decoder(m, ctx_max=64)
+    toks, pm, gm = dec.generate(prompt, 40)
+    ref = oracle.Decoder(m, nranks=1, ctx_max=64)
+    want = ref.generate(prompt, 40)
+    assert list(toks) == list(want)
+    assert pm > 0 and gm > 0
+    # the device's token buffer holds the prompt, then the generated ids
+    tb = dec.tokens()
+    assert list(tb[:7]) == list(prompt) and list(tb[7:47]) == list(want)
+    assert np.array_equal(bits(dec.residual()), bits(ref.residual()))
+    # a second generate on the same decoder starts over
+    toks2, _, _ = dec.generate(prompt, 40)
+    assert list(toks2) == list(want)
+    assert dec.status() == 0
+
+
+@pytest.mark.gpu
+def test_llama_1b_shape_generate(cuda_lib, pkg, oracle):
+    """BASELINE config 3's shapes (random-init Llama-3.2-1B): a 24-token
+    prompt, then greedy tokens, identical to the oracle."""
+    from llm_kv260_b200 import model
+    m = model.synth_model(model.LLAMA_1B, seed=2026)
+    prompt = model.random_prompt(24, model.LLAMA_1B["n_vocab"], seed=7)
+    dec = pkg.Decoder(m, ctx_max=64)
+    toks, _, _ = dec.generate(prompt, 8)
+    ref = oracle.Decoder(m, nranks=1, ctx_max=64)
+    want = ref.generate(prompt, 8)
+    assert list(toks) == list(want)
+    assert np.array_equal(bits(dec.residual()), bits(ref.residual()))
+    assert np.array_equal(bits(dec.logits()), bits(ref.logits()))
+
+
+@pytest.mark.gpu
+def test_decoder_argument_errors(cuda_lib, pkg):
+    from llm_kv260_b200 import model
+    m = model.synth_model(HD64, seed=26)
+    dec = pkg.Decoder(m, ctx_max=16)
+    with pytest.raises(pkg.B200Error):
+        dec.forward(HD64["n_vocab"], 0)          # token out of range
+    with pytest.raises(pkg.B200Error):
+        dec.forward(1, 16)                       # position past ctx_max
+    with pytest.raises(pkg.B200Error):
+        dec.generate(np.zeros(10, np.int32), 8)  # 10 + 8 - 1 > 16
+    bad = dict(m, head_dim=96, n_head=512 // 96)
+    with pytest.raises(pkg.B200Error):
+        pkg.Decoder(bad)
