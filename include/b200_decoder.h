@@ -80,11 +80,19 @@ B200_API int b200_decoder_set_output(b200_decoder_t *d, const void *token_embd, 
  * the token, *value its logit. Every rank must make the same calls. */
 B200_API int b200_decoder_forward(b200_decoder_t *d, int token, int pos, int32_t *pick, float *value);
 
+/* The same loop, queued without waiting (for callers that time or overlap
+ * it): prefill sets the prompt and queues its n_prompt forwards; step queues
+ * n more forwards, each taking the previous pick as its token. Neither waits
+ * for the device; read buffer 2 (the token ids) afterwards. */
+B200_API int b200_decoder_prefill(b200_decoder_t *d, const int32_t *prompt, int n_prompt);
+B200_API int b200_decoder_step(b200_decoder_t *d, int n);
+
 /* runtime::generate with temperature 0 and no end-of-generation token:
  * prompt positions 0..n_prompt-1, then n_gen tokens into out (n_prompt +
- * n_gen - 1 forwards; n_prompt + n_gen - 1 <= ctx_max). prompt_ms and gen_ms
- * (either may be NULL) receive the device time of the prompt's forwards and
- * of the remaining n_gen - 1 forwards. */
+ * n_gen - 1 forwards; n_prompt + n_gen - 1 <= ctx_max). Each token is copied
+ * to the host as it is made. prompt_ms and gen_ms (either may be NULL) receive
+ * the device time of the prompt's forwards and of the generation phase: the
+ * remaining n_gen - 1 forwards and the n_gen token copies. */
 B200_API int b200_decoder_generate(b200_decoder_t *d, const int32_t *prompt, int n_prompt, int n_gen, int32_t *out,
                                    double *prompt_ms, double *gen_ms);
 

@@ -122,6 +122,8 @@ SIGNATURES: dict[str, tuple] = {
     "b200_decoder_set_layer": (c_int, [c_vp, c_int] + [c_vp] * 9),
     "b200_decoder_set_output": (c_int, [c_vp, c_vp, c_vp]),
     "b200_decoder_forward": (c_int, [c_vp, c_int, c_int, P(ctypes.c_int32), P(ctypes.c_float)]),
+    "b200_decoder_prefill": (c_int, [c_vp, c_vp, c_int]),
+    "b200_decoder_step": (c_int, [c_vp, c_int]),
     "b200_decoder_generate": (c_int, [c_vp, c_vp, c_int, c_int, c_vp, P(ctypes.c_double), P(ctypes.c_double)]),
     "b200_decoder_read": (c_int, [c_vp, c_int, c_vp, c_u64]),
     "b200_decoder_status": (c_int, [c_vp, P(c_uint)]),

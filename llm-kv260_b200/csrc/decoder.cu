@@ -96,6 +96,8 @@ struct b200_decoder {
     uint8_t *kv;
     bool output_set;
     cudaGraphExec_t graph;
+    int host_pos;       // where the device loop stands after the work queued so far
+    int32_t *host_io;   // pinned: [0, 2) the pick, [2, 2 + ctx_max + 1) streamed token ids
     Tuning tu;
     // exchange
     uint64_t *win_words[kMaxDecodeRanks];
@@ -313,15 +315,32 @@ int ready(b200_decoder_t *d) {
     return 0;
 }
 
+// The loop's position and prompt length, written on the decoder's stream
+// (the step counter stays as the device left it: the ranks' epochs follow it).
 int set_state(b200_decoder_t *d, int pos, int n_prompt) {
-    DevState host{};
-    if (cudaStreamSynchronize(d->stream) != cudaSuccess ||
-        cudaMemcpy(&host, d->st, sizeof host, cudaMemcpyDeviceToHost) != cudaSuccess)
-        return dfail(kErrCuda, "decoder: state read failed");
-    host.pos = pos;
-    host.n_prompt = n_prompt;
-    if (int rc = h2d(d->st, &host, sizeof host, d->stream)) return rc;
-    return cudaStreamSynchronize(d->stream) == cudaSuccess ? 0 : dfail(kErrCuda, "decoder: state write failed");
+    if (int rc = h2d(&d->st->pos, &pos, 4, d->stream)) return rc;
+    if (int rc = h2d(&d->st->n_prompt, &n_prompt, 4, d->stream)) return rc;
+    d->host_pos = pos;
+    return 0;
+}
+
+int launch_steps(b200_decoder_t *d, int n) {
+    if (n < 0 || d->host_pos + n > d->c.ctx_max)
+        return dfail(kErrInval, "decoder: %d more positions from %d pass ctx_max %d", n, d->host_pos, d->c.ctx_max);
+    for (int i = 0; i < n; ++i)
+        if (cudaGraphLaunch(d->graph, d->stream) != cudaSuccess)
+            return dfail(kErrCuda, "decoder: graph launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    d->host_pos += n;
+    return 0;
+}
+
+int queue_prefill(b200_decoder_t *d, const int32_t *prompt, int n_prompt) {
+    if (!prompt || n_prompt < 1 || n_prompt > d->c.ctx_max) return dfail(kErrInval, "decoder: need 1 <= n_prompt <= ctx_max");
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= d->c.n_vocab) return dfail(kErrInval, "decoder: prompt token out of range");
+    if (int rc = h2d(d->tokens, prompt, 4 * static_cast<size_t>(n_prompt), d->stream)) return rc;
+    if (int rc = set_state(d, 0, n_prompt)) return rc;
+    return launch_steps(d, n_prompt);
 }
 
 int check_status(b200_decoder_t *d) {
@@ -403,6 +422,9 @@ extern "C" int b200_decoder_create(b200_decoder_t **out, const b200_decoder_conf
     if (!rc) rc = dalloc(d, &d->kv, 2 * kv_bytes);
     if (!rc) rc = dalloc(d, &d->output_norm, 4 * static_cast<size_t>(e));
     if (rc) return bail(rc);
+    if (cudaHostAlloc(reinterpret_cast<void **>(&d->host_io), 4 * (static_cast<size_t>(c.ctx_max) + 3),
+                      cudaHostAllocDefault) != cudaSuccess)
+        return bail(dfail(kErrNoMem, "decoder: pinned host buffer allocation failed"));
     cudaMemsetAsync(d->sel_scratch, 0, static_cast<size_t>(tile_select_scratch_bytes()), d->stream);
     cudaMemsetAsync(d->st, 0, sizeof(DevState), d->stream);
     cudaMemsetAsync(d->tokens, 0, 4 * (static_cast<size_t>(c.ctx_max) + 1), d->stream);
@@ -498,15 +520,24 @@ extern "C" int b200_decoder_forward(b200_decoder_t *d, int token, int pos, int32
         return dfail(kErrInval, "decoder: token or position out of range");
     if (int rc = h2d(d->tokens + pos, &token, 4, d->stream)) return rc;
     if (int rc = set_state(d, pos, INT_MAX)) return rc;  // the loop's advance writes no token
-    if (cudaGraphLaunch(d->graph, d->stream) != cudaSuccess) return dfail(kErrCuda, "decoder: graph launch failed");
-    int host[2] = {0, 0};
-    cudaMemcpyAsync(host, d->st->pick, 8, cudaMemcpyDeviceToHost, d->stream);
+    if (int rc = launch_steps(d, 1)) return rc;
+    cudaMemcpyAsync(d->host_io, d->st->pick, 8, cudaMemcpyDeviceToHost, d->stream);
     if (cudaStreamSynchronize(d->stream) != cudaSuccess)
         return dfail(kErrCuda, "decoder: forward failed: %s", cudaGetErrorString(cudaGetLastError()));
     if (int rc = check_status(d)) return rc;
-    if (pick) *pick = host[0];
-    if (value) memcpy(value, &host[1], 4);
+    if (pick) *pick = d->host_io[0];
+    if (value) memcpy(value, &d->host_io[1], 4);
     return 0;
+}
+
+extern "C" int b200_decoder_prefill(b200_decoder_t *d, const int32_t *prompt, int n_prompt) {
+    if (int rc = ready(d)) return rc;
+    return queue_prefill(d, prompt, n_prompt);
+}
+
+extern "C" int b200_decoder_step(b200_decoder_t *d, int n) {
+    if (int rc = ready(d)) return rc;
+    return launch_steps(d, n);
 }
 
 extern "C" int b200_decoder_generate(b200_decoder_t *d, const int32_t *prompt, int n_prompt, int n_gen, int32_t *out,
@@ -514,30 +545,31 @@ extern "C" int b200_decoder_generate(b200_decoder_t *d, const int32_t *prompt, i
     if (int rc = ready(d)) return rc;
     if (!prompt || !out || n_prompt < 1 || n_gen < 1 || n_prompt + n_gen - 1 > d->c.ctx_max)
         return dfail(kErrInval, "decoder: need n_prompt >= 1, n_gen >= 1, n_prompt + n_gen - 1 <= ctx_max");
-    for (int i = 0; i < n_prompt; ++i)
-        if (prompt[i] < 0 || prompt[i] >= d->c.n_vocab) return dfail(kErrInval, "decoder: prompt token out of range");
-    if (int rc = h2d(d->tokens, prompt, 4 * static_cast<size_t>(n_prompt), d->stream)) return rc;
-    if (int rc = set_state(d, 0, n_prompt)) return rc;
     cudaEvent_t ev[3];
     for (auto &x : ev) cudaEventCreate(&x);
     cudaEventRecord(ev[0], d->stream);
-    cudaError_t err = cudaSuccess;
-    for (int i = 0; i < n_prompt && err == cudaSuccess; ++i) err = cudaGraphLaunch(d->graph, d->stream);
+    int rc = queue_prefill(d, prompt, n_prompt);
     cudaEventRecord(ev[1], d->stream);
-    for (int i = 0; i + 1 < n_gen && err == cudaSuccess; ++i) err = cudaGraphLaunch(d->graph, d->stream);
+    // each token goes to the host as it is made (4 bytes a step), as the
+    // reference streams it to its caller (tp_llama.cpp:955)
+    cudaError_t err = cudaSuccess;
+    for (int i = 0; i < n_gen && rc == 0 && err == cudaSuccess; ++i) {
+        if (i > 0) rc = launch_steps(d, 1);
+        if (rc == 0)
+            err = cudaMemcpyAsync(d->host_io + 2 + i, d->tokens + n_prompt + i, 4, cudaMemcpyDeviceToHost, d->stream);
+    }
     cudaEventRecord(ev[2], d->stream);
-    if (err == cudaSuccess)
-        err = cudaMemcpyAsync(out, d->tokens + n_prompt, 4 * static_cast<size_t>(n_gen), cudaMemcpyDeviceToHost,
-                              d->stream);
-    if (err == cudaSuccess) err = cudaStreamSynchronize(d->stream);
+    if (rc == 0 && err == cudaSuccess) err = cudaStreamSynchronize(d->stream);
     float a = 0.0f, b = 0.0f;
-    if (err == cudaSuccess) {
+    if (rc == 0 && err == cudaSuccess) {
         cudaEventElapsedTime(&a, ev[0], ev[1]);
         cudaEventElapsedTime(&b, ev[1], ev[2]);
     }
     for (auto &x : ev) cudaEventDestroy(x);
+    if (rc) return rc;
     if (err != cudaSuccess) return dfail(kErrCuda, "decoder: generate failed: %s", cudaGetErrorString(err));
-    if (int rc = check_status(d)) return rc;
+    if (int r2 = check_status(d)) return r2;
+    memcpy(out, d->host_io + 2, 4 * static_cast<size_t>(n_gen));
     if (prompt_ms) *prompt_ms = a;
     if (gen_ms) *gen_ms = b;
     return 0;
@@ -598,6 +630,7 @@ extern "C" int b200_decoder_destroy(b200_decoder_t *d) {
     if (d->stream) cudaStreamSynchronize(d->stream);
     if (d->graph) cudaGraphExecDestroy(d->graph);
     for (void *p : d->allocs) cudaFree(p);
+    if (d->host_io) cudaFreeHost(d->host_io);
     if (d->stream) cudaStreamDestroy(d->stream);
     delete d;
     return 0;

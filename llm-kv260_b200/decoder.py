@@ -46,6 +46,15 @@ class Decoder:
         check(lib().b200_decoder_forward(self.h, token, pos, ctypes.byref(t), ctypes.byref(v)), "b200_decoder_forward")
         return int(t.value), float(v.value)
 
+    def prefill(self, prompt) -> None:
+        """Queue the prompt's forwards (no wait)."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        check(lib().b200_decoder_prefill(self.h, _p(p), p.shape[0]), "b200_decoder_prefill")
+
+    def step(self, n: int = 1) -> None:
+        """Queue n more forwards of the greedy loop (no wait)."""
+        check(lib().b200_decoder_step(self.h, n), "b200_decoder_step")
+
     def generate(self, prompt, n_gen: int) -> tuple[np.ndarray, float, float]:
         """Greedy generate: (tokens, prompt_ms, gen_ms) -- device time of the
         prompt's forwards and of the remaining n_gen - 1."""

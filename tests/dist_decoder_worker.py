@@ -1,0 +1,71 @@
+"""Worker for tests/test_decoder_gpu.py's tensor-parallel case, one process
+per GPU (run by torchrun): every rank decodes its shard of the same seeded
+model; the residual, each rank's logits and every token must equal the
+oracle's simulation of the same number of ranks, bit for bit."""
+
+from __future__ import annotations
+
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+HD64 = dict(n_layer=2, n_embd=512, n_ff=1024, n_head=8, n_head_kv=2, head_dim=64, n_vocab=1024,
+            rope_base=500000.0, rms_eps=1e-5)
+
+
+def bits(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+def main() -> None:
+    out_dir = sys.argv[1]
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(dev)
+    dist.init_process_group("gloo")
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    from llm_kv260_b200 import model
+    from llm_kv260_b200.comm import OrderedAllReduce
+    from oracle import oracle
+    res = {"forward": True, "generate": True}
+    m = model.synth_model(HD64, seed=31)
+    comm = OrderedAllReduce(rank, world, dev, HD64["n_embd"])
+    dec = pkg.Decoder(m, device=dev, rank=rank, nranks=world, comm=comm, ctx_max=48)
+    ref = oracle.Decoder(m, nranks=world, ctx_max=48)
+    prompt = model.random_prompt(5, HD64["n_vocab"], seed=32)
+    tok = None
+    for i in range(14):
+        inp = int(prompt[i]) if i < len(prompt) else tok
+        tg, vg = dec.forward(inp, i)
+        tr, vr = ref.forward(inp, i)
+        same = (np.array_equal(bits(dec.residual()), bits(ref.residual()))
+                and np.array_equal(bits(dec.logits()), bits(ref.logits(rank)))
+                and tg == tr and np.float32(vg) == np.float32(vr))
+        if not same:
+            res["forward"] = False
+            res["first_bad_position"] = i
+            break
+        tok = tr
+    ref2 = oracle.Decoder(m, nranks=world, ctx_max=48)
+    want = ref2.generate(prompt, 30)
+    got, _, _ = dec.generate(prompt, 30)
+    res["generate"] = list(map(int, got)) == list(map(int, want))
+    res["status"] = dec.status()
+    dist.barrier()
+    dec.close()
+    comm.close()
+    with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as fh:
+        json.dump(res, fh)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -109,3 +109,33 @@ def test_decoder_argument_errors(cuda_lib, pkg):
     bad = dict(m, head_dim=96, n_head=512 // 96)
     with pytest.raises(pkg.B200Error):
         pkg.Decoder(bad)
+
+
+@pytest.mark.gpu
+def test_tensor_parallel_decode_on_two_gpus(cuda_lib, tmp_path):
+    """Two ranks (one process per GPU) exchanging K-split partials inside the
+    o and down GEMVs: bit-exact to the oracle's two-rank simulation."""
+    import json
+    import os
+    import socket
+    import subprocess
+    import sys
+
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs (one process per GPU); this box has fewer")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    env = dict(os.environ, PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2", "--master-addr",
+           "127.0.0.1", "--master-port", str(port), os.path.join(root, "tests", "dist_decoder_worker.py"),
+           str(tmp_path)]
+    proc = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    for r in range(2):
+        with open(tmp_path / f"rank{r}.json") as fh:
+            res = json.load(fh)
+        assert res["forward"] and res["generate"] and res["status"] == 0, res
