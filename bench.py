@@ -306,10 +306,12 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     hp = {k: model[k] for k in ("n_layer", "n_embd", "n_ff", "n_head", "n_head_kv", "head_dim", "n_vocab")}
     if world > 1:
         from llm_kv260_b200 import comm as commmod
-        comm = commmod.OrderedAllReduce(rank, world, local_rank, hp["n_embd"])
+        comm = commmod.OrderedAllReduce(rank, world, local_rank, hp["n_embd"] + 256)
     n_prompt = len(prompt)
     ctx = n_prompt + args.warmup + args.steps + 2
-    dec = pkg.Decoder(model, device=local_rank, rank=rank, nranks=world, comm=comm, ctx_max=ctx)
+    persistent = args.mode == "persistent"
+    dec = pkg.Decoder(model, device=local_rank, rank=rank, nranks=world, comm=comm, ctx_max=ctx,
+                      persistent=persistent)
     host_model = model if (rank == 0 and world == 1 and args.cpu_baseline) else None
     del model
     stream = torch.cuda.ExternalStream(dec.stream, device=f"cuda:{local_rank}")
@@ -390,6 +392,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
             except Exception:
                 traffic = None
         kernels_per_token = 5 * hp["n_layer"] + 1 + (2 if world > 1 else 0)
+        launches = (args.steps if flush_needed else 1) if persistent else kernels_per_token * args.steps
         line = {
             "metric": METRIC, "value": 1e3 / ms_per_step, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
@@ -397,11 +400,14 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
             "config": {"workload": workload(args.model, world), "model": args.model, "global_batch": 1,
                        "prompt": n_prompt, "positions": [n_prompt + args.warmup, n_prompt + args.warmup + args.steps],
                        "parallelism": f"tp{world}", "weight_bytes_per_rank": weight_bytes,
+                       "mode": args.mode + (" (one cooperative kernel per run of tokens)" if persistent
+                                            else " (a CUDA graph of 81 kernels per token)"),
                        "l2": ("flushed before every step (per-rank weights smaller than L2)" if flush_needed
                               else "per-rank weights larger than L2, no flush")},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": traffic,
-                         "kernel": "q4_tile_kernel (Q4_0 x Q8_0 GEMV with the decoder's fused prologues/epilogues)",
+                         "kernel": ("token_kernel GEMV phases (Q4_0 x Q8_0, fused prologues/epilogues)" if persistent
+                                    else "q4_tile_kernel (Q4_0 x Q8_0 GEMV with the decoder's fused prologues/epilogues)"),
                          "per_launch_bytes": gemv_bytes / len(gemvs), "launches_per_step": len(gemvs),
                          "method": "the GEMVs' algorithmic bytes per token / step time (CUDA events on the decoder "
                                    "stream): a lower bound on the GEMV's own rate, as the step also holds attention"
@@ -412,7 +418,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                     "d2h_bytes_per_step": 4, "h2d_bytes_per_call": 4 * n_prompt,
                     "call": "b200_decoder_generate: host prompt in, each token copied to host memory as it is made",
                     "tokens_same_as_timed_run": e2e_same},
-            "gpu_launches": kernels_per_token * args.steps,
+            "gpu_launches": launches,
             "clocks": clocks,
             "status": status,
         }
@@ -431,6 +437,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--model", choices=sorted(MODELS), default="1b")
+    ap.add_argument("--mode", choices=["persistent", "graph"], default="graph",
+                    help="decoder execution: one persistent kernel per run of tokens, or a graph of per-op kernels")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--no-per-gemv", dest="per_gemv", action="store_false",
                     help="skip the per-GEMV table of config 2's shapes")

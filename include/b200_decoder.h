@@ -16,12 +16,14 @@
  * keeps the KV cache in float16 (round to nearest even) where the reference
  * keeps float32.
  *
- * On the device a token is one CUDA graph of 5 kernels per layer + lm_head
- * (RMSNorm, embedding, RoPE + KV store, SiLU, the residual adds and the
- * cross-rank exchange are fused into the GEMVs; the greedy pick into
- * lm_head), and the position, step and token ids live in device memory, so
- * generate() replays the same graph once per position with no host work in
- * between.
+ * On the device (persistent = 0) a token is one CUDA graph of 5 kernels per
+ * layer + lm_head (RMSNorm, embedding, RoPE + KV store, SiLU, the residual
+ * adds and the cross-rank exchange are fused into the GEMVs; the greedy pick
+ * into lm_head); with persistent = 1 one cooperative kernel runs a whole run
+ * of tokens as phases between grid barriers. Either way the position, step
+ * and token ids live in device memory, so the loop needs no host work
+ * between tokens. A decoder whose bounded wait ran out (status non-zero) is
+ * not usable afterwards; destroy it.
  *
  * All functions return 0 or a negative errno value; b200_last_error() says
  * why. Pointers to weights are HOST pointers to the full (unsharded) GGUF
@@ -52,10 +54,12 @@ typedef struct {
     int kv_f16;      /* 1: float16 KV cache (BASELINE's), 0: float32 (the reference's) */
     int round_mode;  /* Q8_0 rounding of the GEMV input: 0 floor(|s|+0.5f) (q4_0.py:96), 1 roundf (tp_llama.cpp:343) */
     int exact_norm;  /* 1: RMSNorm always sums squares sequentially (same bits, slower); 0: only when it matters */
+    int persistent;  /* 1: one persistent kernel runs whole runs of tokens (one CTA per SM, weights streamed
+                        across phase barriers); 0: a CUDA graph of per-op kernels per token. Same bits. */
 } b200_decoder_config_t;
 
 /* One rank's decoder on `device`. nranks > 1 needs `comm`: a communicator of
- * this rank created for at least n_embd floats, with its peers' handles
+ * this rank created for at least n_embd + 2 floats, with its peers' handles
  * imported, used by this decoder only. The shard constraints of load_model
  * apply (tp_llama.cpp:246-247): n_embd, n_embd/nranks and n_ff/nranks
  * multiples of 256 and <= 8192; head_dim 64 or 128; n_head/n_head_kv <= 4. */
@@ -100,8 +104,18 @@ B200_API int b200_decoder_generate(b200_decoder_t *d, const int32_t *prompt, int
  * 0 residual x float32[n_embd], 1 this rank's logits float32[n_vocab/nranks],
  * 2 token ids int32[ctx_max+1], 3 the pick (int32 token, float32 value),
  * 4 the q|k|v rows float32[q+k+v shard rows], 5 the attention output
- * float32[n_embd/nranks], 6 SiLU(gate)*up float32[n_ff/nranks]. */
+ * float32[n_embd/nranks], 6 SiLU(gate)*up float32[n_ff/nranks], 7 the phase
+ * trace (b200_decoder_trace). */
 B200_API int b200_decoder_read(b200_decoder_t *d, int what, void *host, uint64_t bytes);
+
+/* Persistent mode: record a phase trace of the first `tokens` (<= 64) tokens
+ * of each later launch -- per (token, phase, CTA) eight values from the
+ * device global timer in ns: 0 phase start (its barrier passed), 1 x staged,
+ * 2 warpgroup 0's rows done, 3 phase end, 4 and 5 the time warpgroups 0 and 1
+ * waited for weight stages, 6 warpgroup 1's rows done, 7 unused -- read back
+ * as buffer 7 (uint64[tokens][phases][SMs][8]). 0 turns it off. A B200
+ * extension with no reference counterpart. */
+B200_API int b200_decoder_trace(b200_decoder_t *d, int tokens);
 
 /* Device status: bit 1 a weight copy wait ran out, bit 2 a peer wait ran
  * out (the outputs since are not valid). Reading clears it. */

@@ -51,7 +51,7 @@ class b200_decoder_config_t(ctypes.Structure):
     """include/b200_decoder.h"""
     _fields_ = [(n, c_int) for n in ("n_layer", "n_embd", "n_ff", "n_head", "n_head_kv", "head_dim", "n_vocab")] + \
                [("rope_base", ctypes.c_float), ("rms_eps", ctypes.c_float)] + \
-               [(n, c_int) for n in ("ctx_max", "kv_f16", "round_mode", "exact_norm")]
+               [(n, c_int) for n in ("ctx_max", "kv_f16", "round_mode", "exact_norm", "persistent")]
 
 
 SIGNATURES: dict[str, tuple] = {
@@ -127,6 +127,7 @@ SIGNATURES: dict[str, tuple] = {
     "b200_decoder_generate": (c_int, [c_vp, c_vp, c_int, c_int, c_vp, P(ctypes.c_double), P(ctypes.c_double)]),
     "b200_decoder_read": (c_int, [c_vp, c_int, c_vp, c_u64]),
     "b200_decoder_status": (c_int, [c_vp, P(c_uint)]),
+    "b200_decoder_trace": (c_int, [c_vp, c_int]),
     "b200_rope_table": (c_int, [c_vp, c_int, c_int, ctypes.c_float]),
     "b200_decoder_stream": (c_vp, [c_vp]),
     "b200_decoder_destroy": (c_int, [c_vp]),

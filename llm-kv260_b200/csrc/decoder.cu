@@ -97,8 +97,18 @@ struct b200_decoder {
     bool output_set;
     cudaGraphExec_t graph;
     int host_pos;       // where the device loop stands after the work queued so far
-    int32_t *host_io;   // pinned: [0, 2) the pick, [2, 2 + ctx_max + 1) streamed token ids
+    int32_t *host_io;   // pinned, mapped: [0, 2) the pick, [2, 2 + ctx_max + 1) token ids by position
     Tuning tu;
+    // persistent mode
+    bool persistent;
+    TokenPhase *phases;           // device copy of the token's phase list
+    int nphases;
+    unsigned long long *bar_count;
+    int *abort_flag;
+    float2 *cand;
+    int *host_tokens_dev;         // host_io + 2 as a device address
+    uint64_t *trace;              // optional phase trace (b200_decoder_trace)
+    int trace_tokens;
     // exchange
     uint64_t *win_words[kMaxDecodeRanks];
     uint64_t slot_words;
@@ -289,12 +299,131 @@ int enqueue_token(b200_decoder_t *d) {
     return 0;
 }
 
+TokenArgs token_args(const b200_decoder_t *d, int ntokens) {
+    const b200_decoder_config_t &c = d->c;
+    TokenArgs a;
+    a.phases = d->phases;
+    a.nphases = d->nphases;
+    a.ntokens = ntokens;
+    a.res = d->res;
+    a.embd = d->token_embd;
+    a.tokens = d->tokens;
+    a.pos = &d->st->pos;
+    a.step = &d->st->step;
+    a.n_prompt = &d->st->n_prompt;
+    a.pick_out = d->st->pick;
+    a.cand = d->cand;
+    a.logits = d->logits;
+    a.rope_cs = d->rope_cs;
+    a.n_embd = c.n_embd;
+    a.head_dim = c.head_dim;
+    a.q_rows = d->q_rows;
+    a.kv_rows = d->kv_rows;
+    a.ctx_max = c.ctx_max;
+    a.kv_f16 = c.kv_f16;
+    a.group = d->group;
+    a.kvh_local = d->kvh_local;
+    a.vocab_base = d->rank * d->vocab_rows;
+    a.scale = 1.0f / sqrtf(static_cast<float>(c.head_dim));
+    a.eps = c.rms_eps;
+    a.exact_norm = c.exact_norm;
+    a.round_mode = c.round_mode;
+    a.nranks = d->nranks;
+    a.rank = d->rank;
+    for (int r = 0; r < kMaxDecodeRanks; ++r) a.win_words[r] = d->win_words[r];
+    a.slot_words = d->slot_words;
+    a.ar_per_token = 2 * c.n_layer;
+    a.peer_status = d->peer_status;
+    a.bar_count = d->bar_count;
+    a.abort_flag = d->abort_flag;
+    a.status = status_word();
+    a.host_tokens = d->host_tokens_dev;
+    a.trace = d->trace;
+    a.trace_tokens = d->trace_tokens;
+    return a;
+}
+
+// The persistent kernel's phase list for one token (the same ops, in the
+// same order, as enqueue_token).
+int build_phases(b200_decoder_t *d) {
+    const b200_decoder_config_t &c = d->c;
+    const int e = c.n_embd;
+    std::vector<TokenPhase> ph;
+    for (int l = 0; l < c.n_layer; ++l) {
+        const DecLayer &W = d->layers[l];
+        TokenPhase A;
+        A.w = W.qkv;
+        A.rows = d->q_rows + 2 * d->kv_rows;
+        A.k = e;
+        A.pro = l == 0 ? kProEmbedNorm : kProRmsnorm;
+        A.norm_w = W.attn_norm;
+        A.epi = kEpiRopeKv;
+        A.y = d->qkv_y;
+        A.kcache = W.kcache;
+        A.vcache = W.vcache;
+        ph.push_back(A);
+        TokenPhase T;
+        T.kind = kPhAttn;
+        T.kcache = W.kcache;
+        T.vcache = W.vcache;
+        T.q = d->qkv_y;
+        T.out = d->attn;
+        ph.push_back(T);
+        TokenPhase O;
+        O.w = W.o;
+        O.rows = e;
+        O.k = d->o_k;
+        O.x = d->attn;
+        O.epi = kEpiResidual;
+        O.ar_index = 2 * l;
+        ph.push_back(O);
+        TokenPhase U;
+        U.w = W.gateup;
+        U.rows = 2 * d->ff_rows;
+        U.k = e;
+        U.pro = kProRmsnorm;
+        U.norm_w = W.ffn_norm;
+        U.epi = kEpiSiluPairs;
+        U.act = d->act;
+        ph.push_back(U);
+        TokenPhase D;
+        D.w = W.down;
+        D.rows = e;
+        D.k = d->down_k;
+        D.x = d->act;
+        D.epi = kEpiResidual;
+        D.ar_index = 2 * l + 1;
+        ph.push_back(D);
+    }
+    TokenPhase H;
+    H.w = d->lm_head;
+    H.rows = d->vocab_rows;
+    H.k = e;
+    H.pro = kProRmsnorm;
+    H.norm_w = d->output_norm;
+    H.epi = kEpiStore;
+    H.y = d->logits;
+    H.pick = 1;
+    ph.push_back(H);
+    if (static_cast<int>(ph.size()) > kMaxTokenPhases) return dfail(kErrInval, "decoder: too many layers for one token program");
+    if (int rc = dalloc(d, &d->phases, sizeof(TokenPhase) * ph.size())) return rc;
+    if (int rc = h2d(d->phases, ph.data(), sizeof(TokenPhase) * ph.size(), d->stream)) return rc;
+    if (cudaStreamSynchronize(d->stream) != cudaSuccess) return dfail(kErrCuda, "decoder: phase upload failed");
+    d->nphases = static_cast<int>(ph.size());
+    TokenArgs a = token_args(d, 1);
+    int smem = 0, ring = 0, wgs = 0, grid = 0;
+    if (int rc = token_kernel_plan(a, &smem, &ring, &wgs, &grid))
+        return dfail(rc, "decoder: the persistent kernel does not fit this model (context %d too long?)", c.ctx_max);
+    return 0;
+}
+
 int ready(b200_decoder_t *d) {
     if (!d) return dfail(kErrInval, "decoder: null handle");
     for (const DecLayer &L : d->layers)
         if (!L.set) return dfail(kErrInval, "decoder: a layer's weights are not set");
     if (!d->output_set) return dfail(kErrInval, "decoder: token_embd / output_norm not set");
     if (int rc = use_dev(d)) return rc;
+    if (d->persistent) return d->nphases ? 0 : build_phases(d);
     if (d->graph) return 0;
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeRelaxed);
@@ -327,6 +456,13 @@ int set_state(b200_decoder_t *d, int pos, int n_prompt) {
 int launch_steps(b200_decoder_t *d, int n) {
     if (n < 0 || d->host_pos + n > d->c.ctx_max)
         return dfail(kErrInval, "decoder: %d more positions from %d pass ctx_max %d", n, d->host_pos, d->c.ctx_max);
+    if (d->persistent) {
+        if (n == 0) return 0;
+        if (int rc = token_kernel_launch(token_args(d, n), d->stream))
+            return dfail(rc, "decoder: persistent kernel launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+        d->host_pos += n;
+        return 0;
+    }
     for (int i = 0; i < n; ++i)
         if (cudaGraphLaunch(d->graph, d->stream) != cudaSuccess)
             return dfail(kErrCuda, "decoder: graph launch failed: %s", cudaGetErrorString(cudaGetLastError()));
@@ -346,6 +482,11 @@ int queue_prefill(b200_decoder_t *d, const int32_t *prompt, int n_prompt) {
 int check_status(b200_decoder_t *d) {
     unsigned s = 0;
     read_status(&s);
+    if (d->abort_flag) {
+        int ab = 0;
+        cudaMemcpy(&ab, d->abort_flag, 4, cudaMemcpyDeviceToHost);
+        if (ab) s |= kStatusStageTimeout;
+    }
     unsigned ps = 0;
     if (d->peer_status) cudaMemcpy(&ps, d->peer_status, 4, cudaMemcpyDeviceToHost);
     if (s || ps) return dfail(kErrTimeout, "decoder: a bounded wait ran out (status %u, peer status %u)", s, ps);
@@ -423,8 +564,25 @@ extern "C" int b200_decoder_create(b200_decoder_t **out, const b200_decoder_conf
     if (!rc) rc = dalloc(d, &d->output_norm, 4 * static_cast<size_t>(e));
     if (rc) return bail(rc);
     if (cudaHostAlloc(reinterpret_cast<void **>(&d->host_io), 4 * (static_cast<size_t>(c.ctx_max) + 3),
-                      cudaHostAllocDefault) != cudaSuccess)
+                      cudaHostAllocMapped) != cudaSuccess)
         return bail(dfail(kErrNoMem, "decoder: pinned host buffer allocation failed"));
+    d->persistent = c.persistent != 0;
+    if (d->persistent) {
+        void *hd = nullptr;
+        if (cudaHostGetDevicePointer(&hd, d->host_io, 0) != cudaSuccess)
+            return bail(dfail(kErrCuda, "decoder: mapped host buffer has no device address"));
+        d->host_tokens_dev = static_cast<int *>(hd) + 2;
+        const int sms = sm_count();
+        if (sms <= 0) return bail(dfail(kErrNoDev, "decoder: no SM count"));
+        rc = dalloc(d, &d->bar_count, 8);
+        if (!rc) rc = dalloc(d, &d->abort_flag, 4);
+        if (!rc) rc = dalloc(d, &d->cand, sizeof(float2) * static_cast<size_t>(sms));
+        if (rc) return bail(rc);
+        cudaMemsetAsync(d->bar_count, 0, 8, d->stream);
+        cudaMemsetAsync(d->abort_flag, 0, 4, d->stream);
+        if (nranks > 1 && d->slot_words < static_cast<uint64_t>(c.n_embd) + 2)
+            return bail(dfail(kErrInval, "decoder: the communicator needs room for n_embd + 2 floats"));
+    }
     cudaMemsetAsync(d->sel_scratch, 0, static_cast<size_t>(tile_select_scratch_bytes()), d->stream);
     cudaMemsetAsync(d->st, 0, sizeof(DevState), d->stream);
     cudaMemsetAsync(d->tokens, 0, 4 * (static_cast<size_t>(c.ctx_max) + 1), d->stream);
@@ -553,10 +711,16 @@ extern "C" int b200_decoder_generate(b200_decoder_t *d, const int32_t *prompt, i
     // each token goes to the host as it is made (4 bytes a step), as the
     // reference streams it to its caller (tp_llama.cpp:955)
     cudaError_t err = cudaSuccess;
-    for (int i = 0; i < n_gen && rc == 0 && err == cudaSuccess; ++i) {
-        if (i > 0) rc = launch_steps(d, 1);
-        if (rc == 0)
-            err = cudaMemcpyAsync(d->host_io + 2 + i, d->tokens + n_prompt + i, 4, cudaMemcpyDeviceToHost, d->stream);
+    if (d->persistent) {
+        // the kernel writes each token to the mapped host buffer as it makes it
+        if (rc == 0) rc = launch_steps(d, n_gen - 1);
+    } else {
+        for (int i = 0; i < n_gen && rc == 0 && err == cudaSuccess; ++i) {
+            if (i > 0) rc = launch_steps(d, 1);
+            if (rc == 0)
+                err = cudaMemcpyAsync(d->host_io + 2 + n_prompt + i, d->tokens + n_prompt + i, 4,
+                                      cudaMemcpyDeviceToHost, d->stream);
+        }
     }
     cudaEventRecord(ev[2], d->stream);
     if (rc == 0 && err == cudaSuccess) err = cudaStreamSynchronize(d->stream);
@@ -569,9 +733,22 @@ extern "C" int b200_decoder_generate(b200_decoder_t *d, const int32_t *prompt, i
     if (rc) return rc;
     if (err != cudaSuccess) return dfail(kErrCuda, "decoder: generate failed: %s", cudaGetErrorString(err));
     if (int r2 = check_status(d)) return r2;
-    memcpy(out, d->host_io + 2, 4 * static_cast<size_t>(n_gen));
+    memcpy(out, d->host_io + 2 + n_prompt, 4 * static_cast<size_t>(n_gen));
     if (prompt_ms) *prompt_ms = a;
     if (gen_ms) *gen_ms = b;
+    return 0;
+}
+
+extern "C" int b200_decoder_trace(b200_decoder_t *d, int tokens) {
+    if (!d || tokens < 0 || tokens > 64) return dfail(kErrInval, "decoder: trace 0..64 tokens");
+    if (!d->persistent) return dfail(kErrInval, "decoder: the phase trace is the persistent kernel's");
+    if (int rc = ready(d)) return rc;
+    if (tokens > d->trace_tokens) {
+        const int sms = sm_count();
+        if (int rc = dalloc(d, &d->trace, static_cast<size_t>(tokens) * d->nphases * sms * 8 * 8)) return rc;
+    }
+    d->trace_tokens = tokens;
+    if (!tokens) d->trace = nullptr;
     return 0;
 }
 
@@ -588,6 +765,7 @@ extern "C" int b200_decoder_read(b200_decoder_t *d, int what, void *host, uint64
         case 4: src = d->qkv_y; n = 4ull * (d->q_rows + 2 * d->kv_rows); break;
         case 5: src = d->attn; n = 4ull * d->o_k; break;
         case 6: src = d->act; n = 4ull * d->down_k; break;
+        case 7: src = d->trace; n = 8ull * d->trace_tokens * d->nphases * sm_count() * 8; break;
         default: return dfail(kErrInval, "decoder: unknown buffer %d", what);
     }
     if (bytes != n) return dfail(kErrInval, "decoder: buffer %d holds %llu bytes", what, static_cast<unsigned long long>(n));

@@ -20,12 +20,14 @@ class Decoder:
     GGUF loader would): hparams, "layers", "token_embd", "output_norm"."""
 
     def __init__(self, model: dict, device: int = 0, rank: int = 0, nranks: int = 1, comm=None,
-                 ctx_max: int = 512, kv_f16: bool = True, round_mode: int = 0, exact_norm: bool = False):
+                 ctx_max: int = 512, kv_f16: bool = True, round_mode: int = 0, exact_norm: bool = False,
+                 persistent: bool = False):
         c = capi.b200_decoder_config_t()
         for n in ("n_layer", "n_embd", "n_ff", "n_head", "n_head_kv", "head_dim", "n_vocab"):
             setattr(c, n, int(model[n]))
         c.rope_base, c.rms_eps = float(model["rope_base"]), float(model["rms_eps"])
         c.ctx_max, c.kv_f16, c.round_mode, c.exact_norm = ctx_max, int(kv_f16), round_mode, int(exact_norm)
+        c.persistent = int(persistent)
         self.cfg, self.rank, self.nranks, self.ctx_max = c, rank, nranks, ctx_max
         self.h = ctypes.c_void_p()
         check(lib().b200_decoder_create(ctypes.byref(self.h), ctypes.byref(c), device, rank, nranks,
@@ -78,6 +80,16 @@ class Decoder:
 
     def tokens(self) -> np.ndarray:
         return self._read(2, self.ctx_max + 1, np.int32)
+
+    def trace(self, tokens: int) -> None:
+        """Persistent mode: stamp the phases of the first `tokens` tokens of each later launch."""
+        check(lib().b200_decoder_trace(self.h, tokens), "b200_decoder_trace")
+        self._trace_tokens = tokens
+
+    def read_trace(self, nphases: int, sms: int) -> np.ndarray:
+        """[tokens, phases, SMs, 8] trace values (ns) of the last traced launch (b200_decoder_trace)."""
+        t = self._trace_tokens
+        return self._read(7, t * nphases * sms * 8, np.uint64).reshape(t, nphases, sms, 8)
 
     def status(self) -> int:
         s = ctypes.c_uint(0)

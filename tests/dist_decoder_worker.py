@@ -35,33 +35,37 @@ def main() -> None:
     from llm_kv260_b200 import model
     from llm_kv260_b200.comm import OrderedAllReduce
     from oracle import oracle
-    res = {"forward": True, "generate": True}
     m = model.synth_model(HD64, seed=31)
-    comm = OrderedAllReduce(rank, world, dev, HD64["n_embd"])
-    dec = pkg.Decoder(m, device=dev, rank=rank, nranks=world, comm=comm, ctx_max=48)
-    ref = oracle.Decoder(m, nranks=world, ctx_max=48)
     prompt = model.random_prompt(5, HD64["n_vocab"], seed=32)
-    tok = None
-    for i in range(14):
-        inp = int(prompt[i]) if i < len(prompt) else tok
-        tg, vg = dec.forward(inp, i)
-        tr, vr = ref.forward(inp, i)
-        same = (np.array_equal(bits(dec.residual()), bits(ref.residual()))
-                and np.array_equal(bits(dec.logits()), bits(ref.logits(rank)))
-                and tg == tr and np.float32(vg) == np.float32(vr))
-        if not same:
-            res["forward"] = False
-            res["first_bad_position"] = i
-            break
-        tok = tr
-    ref2 = oracle.Decoder(m, nranks=world, ctx_max=48)
-    want = ref2.generate(prompt, 30)
-    got, _, _ = dec.generate(prompt, 30)
-    res["generate"] = list(map(int, got)) == list(map(int, want))
-    res["status"] = dec.status()
-    dist.barrier()
-    dec.close()
-    comm.close()
+    res = {}
+    for mode in ("graph", "persistent"):
+        r = {"forward": True, "generate": True}
+        comm = OrderedAllReduce(rank, world, dev, HD64["n_embd"] + 256)
+        dec = pkg.Decoder(m, device=dev, rank=rank, nranks=world, comm=comm, ctx_max=48,
+                          persistent=mode == "persistent")
+        ref = oracle.Decoder(m, nranks=world, ctx_max=48)
+        tok = None
+        for i in range(14):
+            inp = int(prompt[i]) if i < len(prompt) else tok
+            tg, vg = dec.forward(inp, i)
+            tr, vr = ref.forward(inp, i)
+            same = (np.array_equal(bits(dec.residual()), bits(ref.residual()))
+                    and np.array_equal(bits(dec.logits()), bits(ref.logits(rank)))
+                    and tg == tr and np.float32(vg) == np.float32(vr))
+            if not same:
+                r["forward"] = False
+                r["first_bad_position"] = i
+                break
+            tok = tr
+        ref2 = oracle.Decoder(m, nranks=world, ctx_max=48)
+        want = ref2.generate(prompt, 30)
+        got, _, _ = dec.generate(prompt, 30)
+        r["generate"] = list(map(int, got)) == list(map(int, want))
+        r["status"] = dec.status()
+        dist.barrier()
+        dec.close()
+        comm.close()
+        res[mode] = r
     with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as fh:
         json.dump(res, fh)
     dist.destroy_process_group()

@@ -38,32 +38,39 @@ def step_by_step(pkg, oracle, hp, seed, n_prompt, n_steps, ctx_max=64, **kw):
     ref.close()
 
 
+MODES = pytest.mark.parametrize("persistent", [False, True], ids=["graph", "persistent"])
+
+
 @pytest.mark.gpu
+@MODES
 @pytest.mark.parametrize("kw", [dict(), dict(kv_f16=False), dict(round_mode=1), dict(exact_norm=True)],
                          ids=["f16kv", "f32kv", "roundf", "exact_norm"])
-def test_forward_bit_exact_hd64(cuda_lib, pkg, oracle, kw):
-    step_by_step(pkg, oracle, HD64, seed=21, n_prompt=5, n_steps=12, **kw)
+def test_forward_bit_exact_hd64(cuda_lib, pkg, oracle, kw, persistent):
+    step_by_step(pkg, oracle, HD64, seed=21, n_prompt=5, n_steps=12, persistent=persistent, **kw)
 
 
 @pytest.mark.gpu
-def test_forward_bit_exact_hd128_group3(cuda_lib, pkg, oracle):
-    step_by_step(pkg, oracle, HD128, seed=22, n_prompt=4, n_steps=10)
+@MODES
+def test_forward_bit_exact_hd128_group3(cuda_lib, pkg, oracle, persistent):
+    step_by_step(pkg, oracle, HD128, seed=22, n_prompt=4, n_steps=10, persistent=persistent)
 
 
 @pytest.mark.gpu
-def test_long_context_crosses_attention_chunks(cuda_lib, pkg, oracle):
+@MODES
+def test_long_context_crosses_attention_chunks(cuda_lib, pkg, oracle, persistent):
     """More positions than one 128-position V chunk, and a tail that is not a
     multiple of 4 (softmax's scalar tail)."""
     hp = dict(HD64, n_layer=1)
-    step_by_step(pkg, oracle, hp, seed=23, n_prompt=290, n_steps=291, ctx_max=300)
+    step_by_step(pkg, oracle, hp, seed=23, n_prompt=290, n_steps=291, ctx_max=300, persistent=persistent)
 
 
 @pytest.mark.gpu
-def test_generate_matches_oracle(cuda_lib, pkg, oracle):
+@MODES
+def test_generate_matches_oracle(cuda_lib, pkg, oracle, persistent):
     from llm_kv260_b200 import model
     m = model.synth_model(HD64, seed=24)
     prompt = model.random_prompt(7, HD64["n_vocab"], seed=25)
-    dec = pkg.Decoder(m, ctx_max=64)
+    dec = pkg.Decoder(m, ctx_max=64, persistent=persistent)
     toks, pm, gm = dec.generate(prompt, 40)
     ref = oracle.Decoder(m, nranks=1, ctx_max=64)
     want = ref.generate(prompt, 40)
@@ -80,13 +87,14 @@ def test_generate_matches_oracle(cuda_lib, pkg, oracle):
 
 
 @pytest.mark.gpu
-def test_llama_1b_shape_generate(cuda_lib, pkg, oracle):
+@MODES
+def test_llama_1b_shape_generate(cuda_lib, pkg, oracle, persistent):
     """BASELINE config 3's shapes (random-init Llama-3.2-1B): a 24-token
     prompt, then greedy tokens, identical to the oracle."""
     from llm_kv260_b200 import model
     m = model.synth_model(model.LLAMA_1B, seed=2026)
     prompt = model.random_prompt(24, model.LLAMA_1B["n_vocab"], seed=7)
-    dec = pkg.Decoder(m, ctx_max=64)
+    dec = pkg.Decoder(m, ctx_max=64, persistent=persistent)
     toks, _, _ = dec.generate(prompt, 8)
     ref = oracle.Decoder(m, nranks=1, ctx_max=64)
     want = ref.generate(prompt, 8)
@@ -109,6 +117,9 @@ def test_decoder_argument_errors(cuda_lib, pkg):
     bad = dict(m, head_dim=96, n_head=512 // 96)
     with pytest.raises(pkg.B200Error):
         pkg.Decoder(bad)
+    pd = pkg.Decoder(m, ctx_max=16, persistent=True)
+    with pytest.raises(pkg.B200Error):
+        pd.step(17)                              # past ctx_max from position 0
 
 
 @pytest.mark.gpu
@@ -138,4 +149,5 @@ def test_tensor_parallel_decode_on_two_gpus(cuda_lib, tmp_path):
     for r in range(2):
         with open(tmp_path / f"rank{r}.json") as fh:
             res = json.load(fh)
-        assert res["forward"] and res["generate"] and res["status"] == 0, res
+        for mode in ("graph", "persistent"):
+            assert res[mode]["forward"] and res[mode]["generate"] and res[mode]["status"] == 0, (mode, res)
