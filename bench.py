@@ -251,7 +251,7 @@ def per_gemv_table(pkg, torch, world: int, device: int, launches: int = 200) -> 
     eng = pkg.Engine(device, stream=0)
     stream = torch.cuda.Stream(device)
     eng.set_stream(stream.cuda_stream)
-    eng.configure(fuse_quantize=1, pdl=1, stages=4, ctas_per_sm=4, kslices=1)
+    eng.configure(fuse_quantize=1, pdl=1, stages=8, ctas_per_sm=4, kslices=1)
     dev = f"cuda:{device}"
     x = torch.randn(8192, dtype=torch.float32, device=dev)
     out = {}

@@ -529,7 +529,7 @@ extern "C" int b200_decoder_create(b200_decoder_t **out, const b200_decoder_conf
     d->heads_local = c.n_head / nranks;
     d->kvh_local = c.n_head_kv / nranks;
     d->group = c.n_head / c.n_head_kv;
-    d->tu.stages = 4;
+    d->tu.stages = 8;
     d->tu.ctas_per_sm = 4;
     d->tu.kslices = 1;
     d->layers.resize(c.n_layer);

@@ -7,25 +7,23 @@
 // does the same for HBM. Rows are padded to a multiple of 16. For row group
 // g (rows 16g..16g+15) and chunk c (blocks 8c..8c+7) a 2304-byte tile sits at
 // byte ((g * nch) + c) * 2304:
-//     [0, 2048)     nibbles: 16 bytes for lane l, row i at (l * 16 + i) * 16
-//     [2048, 2304)  scales:  float16 bits for lane l, row i at 2048 + (l * 16 + i) * 2
+//     [0, 2048)     nibbles: 16 bytes for row i, lane l at (i * 8 + l) * 16
+//     [2048, 2304)  scales:  float16 bits for row i, lane l at 2048 + (i * 8 + l) * 2
 // The 16 nibble bytes of a block are copied unchanged (byte j: weight j in
 // the low nibble, weight j+16 in the high one), so the bytes per weight stay
 // 18/32 and the algorithmic traffic is the GGUF file's.
 //
-// Kernel. A CTA owns whole 16-row groups. Thread (s, l, i) -- K-slice s,
-// lane l, row i -- computes the block terms of lane l of row i for the chunks
-// of slice s (at most 8, so its x blocks stay in registers). With one slice
-// (K <= 2048) the thread adds its terms straight into the lane chain; with
-// several, the terms go to shared memory and slice 0 then runs each lane's
-// chain over all chunks in order -- the float adds stay sequential exactly as
-// q4_0.py:177-179 orders them, only the block dots run in parallel. A stage is
-// one row group's whole tile run, moved by ONE 1-D bulk copy (TMA engine, no
-// multicast) into an mbarrier ring, issued before the kernel waits on its
-// predecessor (programmatic dependent launch). Every block is one conflict-
-// free 128-bit shared load (a warp reads 512 contiguous bytes) plus a 16-bit
-// scale load and 8 __dp4a; all warps run identical code. Per row group the 8
-// lane sums meet in tree_sum's order.
+// Kernel. One producer warp streams whole row groups (one group's tile run =
+// one 1-D bulk copy, TMA engine, no multicast) into a ring of shared-memory
+// stages, issued before the kernel waits on its predecessor (programmatic
+// dependent launch). Two consumer warp-quads take every other group; in a
+// quad, warp w owns rows 4w..4w+3 and thread (row i, lane l) runs lane l's
+// chain of row i over all chunks in order (q4_0.py:177-179) -- its x blocks
+// in registers when K <= 2048. A warp reads its 4 rows' 512 contiguous bytes
+// per chunk (conflict-free), meets the 8 lane sums with xor shuffles 1, 2, 4
+// -- tree_sum's pairing (q4_0.py:67-78), IEEE addition being commutative --
+// and frees its stage with one mbarrier arrival: no CTA-wide barrier per
+// stage, so the quads and the producer run independently.
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -35,13 +33,14 @@ namespace b200 {
 
 namespace {
 
-constexpr int kTileThreads = kTileRows * kLanes;   // threads per K-slice: 128
-constexpr int kTileNibBytes = kTileThreads * 16;   // 2048
+constexpr int kQuadThreads = kTileRows * kLanes;  // one 16-row group: 4 warps, 128 threads
+constexpr int kQuads = 2;                          // groups in flight per CTA
+constexpr int kConsumers = kQuads * kQuadThreads;  // 256
+constexpr int kTileThreads = kConsumers + 32;      // + the producer warp
+constexpr int kTileNibBytes = kQuadThreads * 16;   // 2048
 constexpr int kMaxStages = 8;
-constexpr int kBarBytes = 64;
-constexpr int kRedBytes = 2 * kTileThreads * 4;    // double-buffered lane sums
 constexpr int kSmemAlign = 128;
-constexpr int kMaxCps = 8;                         // chunks per K-slice (x blocks in registers)
+constexpr int kXregChunks = 8;                     // K <= 2048: x blocks in registers
 constexpr int kSelMaxCtas = 4096;                  // fused greedy pick: candidate slots
 
 struct TileParams {
@@ -130,16 +129,16 @@ __device__ __noinline__ void stage_x_norm(const TileParams &p, uint8_t *xs, floa
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(kFullMask, ss, off));
     if (lane == 0) dred[warp] = ss;
-    __syncthreads();
+    named_sync(1, kConsumers);
     if (threadIdx.x == 0) {
         double tot = 0.0;
-        for (int w = 0; w < static_cast<int>(blockDim.x / 32); ++w) tot = __dadd_rn(tot, dred[w]);
+        for (int w = 0; w < kConsumers / 32; ++w) tot = __dadd_rn(tot, dred[w]);
         const double q = __ddiv_rn(tot, static_cast<double>(k));
         const float f = __double2float_rn(q);
         s_exact = p.dec.exact_norm || !rms_float_is_safe(q, f, k);
         s_f = f;
     }
-    __syncthreads();
+    named_sync(1, kConsumers);
     if (s_exact) {
         // tp_llama.cpp:560-564: lane j sums x[i]^2 for i = j, j+4, ... in order
         if (threadIdx.x < 4) {
@@ -148,12 +147,12 @@ __device__ __noinline__ void stage_x_norm(const TileParams &p, uint8_t *xs, floa
                 a = __dadd_rn(a, __dmul_rn(static_cast<double>(xf[i]), static_cast<double>(xf[i])));
             dred[threadIdx.x] = a;
         }
-        __syncthreads();
+        named_sync(1, kConsumers);
         if (threadIdx.x == 0) {
             const double ss2 = __dadd_rn(__dadd_rn(dred[0], dred[2]), __dadd_rn(dred[1], dred[3]));
             s_f = __double2float_rn(__ddiv_rn(ss2, static_cast<double>(k)));
         }
-        __syncthreads();
+        named_sync(1, kConsumers);
     }
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s_f, p.dec.eps)));
     if (b < nb) {
@@ -189,63 +188,101 @@ __device__ __forceinline__ bool sel_better(float av, int ai, float bv, int bi) {
     return av > bv || (av == bv && ai < bi);
 }
 
-__device__ __forceinline__ void issue_group(const TileParams &p, uint64_t *bars, uint8_t *ring, int g, int s,
-                                            uint64_t policy) {
-    const int slot = s % p.stages;
-    mbar_arrive_expect_tx(&bars[slot], static_cast<uint32_t>(p.slot_bytes));
-    bulk_g2s(ring + slot * p.slot_bytes, p.w + static_cast<size_t>(g) * p.slot_bytes,
-             static_cast<uint32_t>(p.slot_bytes), &bars[slot], policy);
-}
-
-// Block term of tile `tile` (one chunk of the row group) for this thread's
-// (lane, row) slot u = lane * 16 + row.
-__device__ __forceinline__ float tile_term(const uint8_t *tile, int u, const XBlock &xb) {
+// Block term of one chunk-tile for row i, lane l.
+__device__ __forceinline__ float tile_term(const uint8_t *tile, int i, int l, const XBlock &xb) {
+    const int u = i * kLanes + l;
     const uint4 nv = *reinterpret_cast<const uint4 *>(tile + u * 16);
     const uint32_t db = *reinterpret_cast<const uint16_t *>(tile + kTileNibBytes + u * 2);
     const uint32_t n[4] = {nv.x, nv.y, nv.z, nv.w};
     return block_term_words(n, db, xb);
 }
 
-// CPS: chunks per K-slice; KS: K-slices (threads = 128 * KS); KS * CPS >= nch.
-template <int XMODE, int CPS, int KS>
-__global__ void __launch_bounds__(kTileThreads * KS) q4_tile_kernel(const __grid_constant__ TileParams p) {
+// Bounded ring wait: gives up when another thread of the CTA gave up, or
+// after kStageTimeoutNs (then marks the status and the CTA's abort flag).
+__device__ __forceinline__ bool ring_wait(uint64_t *bar, uint32_t parity, unsigned *status, volatile int *abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (unsigned spin = 0;; ++spin) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((spin & 255u) == 255u) {
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > kStageTimeoutNs) {
+                atomicOr(status, kStatusStageTimeout);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// XREG: K <= 2048, each thread's 8 x blocks stay in registers.
+template <int XMODE, bool XREG>
+__global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_constant__ TileParams p) {
     extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t full[kMaxStages], empty[kMaxStages];
     __shared__ int s_abort;
+    __shared__ unsigned s_last;
+    __shared__ float2 s_best[kConsumers / kLanes];
     uint8_t *ring = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + kSmemAlign - 1) & ~static_cast<uintptr_t>(kSmemAlign - 1));
-    uint8_t *after = ring + p.stages * p.slot_bytes;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(after);
-    float *red = reinterpret_cast<float *>(after + kBarBytes);
-    float *tv = reinterpret_cast<float *>(after + kBarBytes + kRedBytes);  // [nch][128], KS > 1 only
-    uint8_t *xs = after + kBarBytes + kRedBytes + (KS > 1 ? p.nch * kTileThreads * 4 : 0);
+    uint8_t *xs = ring + p.stages * p.slot_bytes;
 
-    const int t = threadIdx.x, slice = t / kTileThreads, u = t % kTileThreads, L = u / kTileRows;
+    const int t = threadIdx.x, warp = t / 32, lane = t % 32;
     const int g0 = static_cast<int>(static_cast<long long>(p.groups) * blockIdx.x / gridDim.x);
     const int g1 = static_cast<int>(static_cast<long long>(p.groups) * (blockIdx.x + 1) / gridDim.x);
-    const int S = p.stages;
-    const int nst = g1 - g0;
+    const int S = p.stages, nst = g1 - g0;
 
     if (t == 0) {
         s_abort = 0;
-        for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kQuadThreads / 32);
+        }
         fence_mbar_init();
     }
     __syncthreads();
-    const uint64_t policy = make_policy(p.l2_policy);
-    // The weights do not depend on the previous kernel: start them moving,
-    // let the next kernel launch, then wait for x.
-    if (t == 0)
-        for (int s = 0; s < nst && s < S; ++s) issue_group(p, bars, ring, g0 + s, s, policy);
     pdl_launch_dependents();
-    pdl_wait_prior_grid();
 
-    // One thread per x block: 128*KS threads >= 8*nch blocks, as KS >= nch/8.
+    if (warp == kConsumers / 32) {
+        // producer: the weights do not depend on the previous kernel
+        if (lane == 0) {
+            const uint64_t policy = make_policy(p.l2_policy);
+            int s = 0;
+            for (; s < nst; ++s) {
+                const int slot = s % S;
+                const uint32_t use = static_cast<uint32_t>(s / S);
+                if (use > 0 && !ring_wait(&empty[slot], (use & 1u) ^ 1u, p.status, &s_abort)) break;
+                mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(p.slot_bytes));
+                bulk_g2s(ring + static_cast<size_t>(slot) * p.slot_bytes,
+                         p.w + static_cast<size_t>(g0 + s) * p.slot_bytes, static_cast<uint32_t>(p.slot_bytes),
+                         &full[slot], policy);
+            }
+            // leave only after this CTA's copies have landed (at once when the
+            // consumers took them all; after an abort, each wait bounded)
+            for (int r = s > S ? s - S : 0; r < s; ++r) {
+                const uint64_t t0 = globaltimer_ns();
+                while (!mbar_try_wait(&full[r % S], static_cast<uint32_t>((r / S) & 1)))
+                    if (globaltimer_ns() - t0 > kStageTimeoutNs) break;
+            }
+        }
+        return;
+    }
+
+    pdl_wait_prior_grid();
     if (XMODE == kXF32 && p.dec.pro != kProPlain)
         stage_x_norm(p, xs, reinterpret_cast<float *>(xs + xarea_bytes(p.k)),
                      reinterpret_cast<double *>(xs + xarea_bytes(p.k) + 4 * p.k));
     else
         stage_x<XMODE>(p.x, p.k, p.round_mode, xs);
-    __syncthreads();
+    named_sync(1, kConsumers);
+
+    const int quad = warp / 4, i = (warp % 4) * 4 + (lane >> 3), l = lane & 7;
+    XBlock xr[XREG ? kXregChunks : 1];
+    if constexpr (XREG) {
+#pragma unroll
+        for (int c = 0; c < kXregChunks; ++c)
+            if (c < p.nch) load_xblock_smem(xs, p.k, 8 * c + l, xr[c]);
+    }
     const int epi = p.dec.epi;
     const int dpos = (epi == kEpiRopeKv) ? *p.dec.pos : 0;
     const bool xchg = epi == kEpiResidual && p.dec.nranks > 1;
@@ -255,108 +292,95 @@ __global__ void __launch_bounds__(kTileThreads * KS) q4_tile_kernel(const __grid
         epoch = *p.dec.step * static_cast<uint32_t>(p.dec.ar_per_token) + static_cast<uint32_t>(p.dec.ar_index) + 1u;
         slot_off = static_cast<uint64_t>(epoch & 1u) * kMaxDecodeRanks * p.dec.slot_words;
     }
-    const int c_first = slice * CPS;
-    XBlock xr[CPS];
-#pragma unroll
-    for (int j = 0; j < CPS; ++j)
-        if (c_first + j < p.nch) load_xblock_smem(xs, p.k, 8 * (c_first + j) + L, xr[j]);
 
     float best_v = __int_as_float(0x7fc00000);  // NaN: loses to any number
     int best_i = 0x7fffffff;
-    int s = 0;
-    for (; s < nst; ++s) {
+    bool ok = true;
+    for (int s = quad; s < nst; s += kQuads) {
         const int slot = s % S;
-        if (!wait_stage(&bars[slot], static_cast<uint32_t>((s / S) & 1), p.status)) s_abort = 1;
-        const uint8_t *tiles = ring + slot * p.slot_bytes;
-        float *rbuf = red + (s & 1) * kTileThreads;
-        if constexpr (KS == 1) {
-            float acc = 0.0f;
+        if (!ring_wait(&full[slot], static_cast<uint32_t>((s / S) & 1), p.status, &s_abort)) {
+            ok = false;
+            break;
+        }
+        const uint8_t *tiles = ring + static_cast<size_t>(slot) * p.slot_bytes;
+        float acc = 0.0f;
+        if constexpr (XREG) {
 #pragma unroll
-            for (int j = 0; j < CPS; ++j)
-                if (j < p.nch) acc = __fadd_rn(acc, tile_term(tiles + j * kTileBytes, u, xr[j]));
-            rbuf[u] = acc;
+            for (int c = 0; c < kXregChunks; ++c)
+                if (c < p.nch) acc = __fadd_rn(acc, tile_term(tiles + c * kTileBytes, i, l, xr[c]));
         } else {
-#pragma unroll
-            for (int j = 0; j < CPS; ++j) {
-                const int c = c_first + j;
-                if (c < p.nch) tv[c * kTileThreads + u] = tile_term(tiles + c * kTileBytes, u, xr[j]);
-            }
-            __syncthreads();
-            if (slice == 0) {
-                // lane chain over all chunks, in order (q4_0.py:177-179)
-                float acc = 0.0f;
-                for (int c = 0; c < p.nch; ++c) acc = __fadd_rn(acc, tv[c * kTileThreads + u]);
-                rbuf[u] = acc;
+#pragma unroll 4
+            for (int c = 0; c < p.nch; ++c) {
+                XBlock xb;
+                load_xblock_smem(xs, p.k, 8 * c + l, xb);
+                acc = __fadd_rn(acc, tile_term(tiles + c * kTileBytes, i, l, xb));
             }
         }
-        __syncthreads();
-        if (s_abort) break;
-        if (t == 0 && s + S < nst) issue_group(p, bars, ring, g0 + s + S, s + S, policy);
-        if (t < kTileRows) {
-            const float *r = rbuf + t;
-            const float yv = tree8(r[0 * kTileRows], r[1 * kTileRows], r[2 * kTileRows], r[3 * kTileRows],
-                                   r[4 * kTileRows], r[5 * kTileRows], r[6 * kTileRows], r[7 * kTileRows]);
-            const int row = (g0 + s) * kTileRows + t;
-            const bool live = row < p.rows;
-            if (epi == kEpiStore) {
-                if (live) {
-                    p.y[row] = yv;
-                    if (sel_better(yv, row, best_v, best_i)) {
-                        best_v = yv;
-                        best_i = row;
-                    }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        // tree_sum (q4_0.py:67-78): ((l0+l1)+(l2+l3))+((l4+l5)+(l6+l7))
+        acc = __fadd_rn(acc, __shfl_xor_sync(kFullMask, acc, 1));
+        acc = __fadd_rn(acc, __shfl_xor_sync(kFullMask, acc, 2));
+        const float yv = __fadd_rn(acc, __shfl_xor_sync(kFullMask, acc, 4));
+        const int row = (g0 + s) * kTileRows + i;
+        const bool live = row < p.rows && l == 0;
+        if (epi == kEpiStore) {
+            if (live) {
+                p.y[row] = yv;
+                if (sel_better(yv, row, best_v, best_i)) {
+                    best_v = yv;
+                    best_i = row;
                 }
-            } else if (epi == kEpiRopeKv) {
-                // q and k rows start at multiples of head_dim (even), and a row
-                // group at a multiple of 16, so rope's pair (2i, 2i+1) is this
-                // thread and its neighbour t ^ 1
-                const float other = __shfl_xor_sync(0x0000ffffu, yv, 1);
-                if (live) {
-                    const int hd = p.dec.head_dim, k0 = p.dec.q_rows, v0 = k0 + p.dec.kv_rows;
-                    float out = yv;
-                    if (row < v0) {
-                        const int i = (row % hd) >> 1;
-                        const float *cs = p.dec.rope_cs + static_cast<size_t>(dpos) * hd;
-                        const bool even = !(row & 1);
-                        out = rope_pair(even ? yv : other, even ? other : yv, cs[2 * i], cs[2 * i + 1], even);
-                    }
-                    p.y[row] = out;
-                    if (row >= k0) {
-                        const bool isk = row < v0;
-                        const int rr = row - (isk ? k0 : v0);
-                        const size_t at = (static_cast<size_t>(rr / hd) * p.dec.ctx_max + dpos) * hd + rr % hd;
-                        void *cache = isk ? p.dec.kcache : p.dec.vcache;
-                        if (p.dec.kv_f16)
-                            static_cast<__half *>(cache)[at] = __float2half_rn(out);
-                        else
-                            static_cast<float *>(cache)[at] = out;
-                    }
+            }
+        } else if (epi == kEpiRopeKv) {
+            // q and k rows start at multiples of head_dim (even): rope's pair
+            // (2j, 2j+1) is rows i and i ^ 1, lanes 8 apart
+            const float other = __shfl_xor_sync(kFullMask, yv, 8);
+            if (live) {
+                const int hd = p.dec.head_dim, k0 = p.dec.q_rows, v0 = k0 + p.dec.kv_rows;
+                float out = yv;
+                if (row < v0) {
+                    const int j = (row % hd) >> 1;
+                    const float *cs = p.dec.rope_cs + static_cast<size_t>(dpos) * hd;
+                    const bool even = !(row & 1);
+                    out = rope_pair(even ? yv : other, even ? other : yv, cs[2 * j], cs[2 * j + 1], even);
                 }
-            } else if (epi == kEpiSiluPairs) {
-                const float other = __shfl_xor_sync(0x0000ffffu, yv, 1);
-                if (live) {
-                    if (p.y) p.y[row] = yv;
-                    if (!(row & 1)) p.dec.act[row >> 1] = silu_mul(yv, other);
+                p.y[row] = out;
+                if (row >= k0) {
+                    const bool isk = row < v0;
+                    const int rr = row - (isk ? k0 : v0);
+                    const size_t at = (static_cast<size_t>(rr / hd) * p.dec.ctx_max + dpos) * hd + rr % hd;
+                    void *cache = isk ? p.dec.kcache : p.dec.vcache;
+                    if (p.dec.kv_f16)
+                        static_cast<__half *>(cache)[at] = __float2half_rn(out);
+                    else
+                        static_cast<float *>(cache)[at] = out;
                 }
-            } else if (live) {  // kEpiResidual
+            }
+        } else if (epi == kEpiSiluPairs) {
+            const float other = __shfl_xor_sync(kFullMask, yv, 8);
+            if (live) {
                 if (p.y) p.y[row] = yv;
-                if (!xchg) {
-                    p.dec.res[row] = __fadd_rn(p.dec.res[row], yv);
-                } else {
-                    const uint64_t word = (static_cast<uint64_t>(epoch) << 32) | __float_as_uint(yv);
-                    const uint64_t at = slot_off + static_cast<uint64_t>(p.dec.rank) * p.dec.slot_words + row;
-                    for (int r = 0; r < p.dec.nranks; ++r) st_word(p.dec.win_words[r] + at, word);
-                }
+                if (!(row & 1)) p.dec.act[row >> 1] = silu_mul(yv, other);
+            }
+        } else if (live) {  // kEpiResidual
+            if (p.y) p.y[row] = yv;
+            if (!xchg) {
+                p.dec.res[row] = __fadd_rn(p.dec.res[row], yv);
+            } else {
+                const uint64_t word = (static_cast<uint64_t>(epoch) << 32) | __float_as_uint(yv);
+                const uint64_t at = slot_off + static_cast<uint64_t>(p.dec.rank) * p.dec.slot_words + row;
+                for (int r = 0; r < p.dec.nranks; ++r) st_word(p.dec.win_words[r] + at, word);
             }
         }
     }
-    if (xchg && t < kTileRows && !s_abort) {
+    if (xchg && ok && l == 0) {
         // Every rank computed these rows' partials for its K slice; collect
         // them from this rank's window and sum in rank order
         // (tp_llama.cpp:515-521), then add into the residual (add_into).
         const uint64_t *own = p.dec.win_words[p.dec.rank] + slot_off;
-        for (int s2 = 0; s2 < nst; ++s2) {
-            const int row = (g0 + s2) * kTileRows + t;
+        for (int s = quad; s < nst; s += kQuads) {
+            const int row = (g0 + s) * kTileRows + i;
             if (row >= p.rows) continue;
             float val[kMaxDecodeRanks];
             unsigned pending = (1u << p.dec.nranks) - 1u;
@@ -382,25 +406,35 @@ __global__ void __launch_bounds__(kTileThreads * KS) q4_tile_kernel(const __grid
         }
     }
     if (p.sel_out) {
-        // CTA best over the 16 tree threads (lanes 0..15 of warp 0), then the
-        // last CTA to finish reduces all CTAs' bests.
+        // CTA best over the row threads (l == 0), then the last CTA to finish
+        // reduces all CTAs' bests
+        if (l == 0) s_best[t / kLanes] = make_float2(best_v, __int_as_float(best_i));
+        named_sync(1, kConsumers);
         if (t < 32) {
-            for (int off = 8; off > 0; off >>= 1) {
-                const float ov = __shfl_down_sync(kFullMask, best_v, off, 16);
-                const int oi = __shfl_down_sync(kFullMask, best_i, off, 16);
-                if (sel_better(ov, oi, best_v, best_i)) {
-                    best_v = ov;
-                    best_i = oi;
+            float bv = __int_as_float(0x7fc00000);
+            int bi = 0x7fffffff;
+            for (int c = t; c < kConsumers / kLanes; c += 32) {
+                const float2 cd = s_best[c];
+                if (sel_better(cd.x, __float_as_int(cd.y), bv, bi)) {
+                    bv = cd.x;
+                    bi = __float_as_int(cd.y);
                 }
             }
+            for (int off = 16; off > 0; off >>= 1) {
+                const float ov = __shfl_down_sync(kFullMask, bv, off);
+                const int oi = __shfl_down_sync(kFullMask, bi, off);
+                if (sel_better(ov, oi, bv, bi)) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+            if (t == 0) {
+                p.sel_cand[blockIdx.x] = make_float2(bv, __int_as_float(bi));
+                __threadfence();
+                s_last = atomicAdd(p.sel_ticket, 1u) == gridDim.x - 1;
+            }
         }
-        __shared__ unsigned s_last;
-        if (t == 0) {
-            p.sel_cand[blockIdx.x] = make_float2(best_v, __int_as_float(best_i));
-            __threadfence();
-            s_last = atomicAdd(p.sel_ticket, 1u) == gridDim.x - 1;
-        }
-        __syncthreads();
+        named_sync(1, kConsumers);
         if (s_last && t < 32) {
             __threadfence();
             float bv = __int_as_float(0x7fc00000);
@@ -440,12 +474,6 @@ __global__ void __launch_bounds__(kTileThreads * KS) q4_tile_kernel(const __grid
             }
         }
     }
-    if (s < nst && t == 0) {
-        // Aborted on a stage timeout: let copies already in flight land (each
-        // wait bounded) before the CTA's shared memory goes away.
-        for (int r = s; r < nst && r < s + S; ++r)
-            (void)wait_stage(&bars[r % S], static_cast<uint32_t>((r / S) & 1), p.status);
-    }
 }
 
 // GGUF rows -> tiles; one thread per (row, block), padded rows become zeros.
@@ -468,34 +496,16 @@ __global__ void repack_tiles_kernel(const uint8_t *__restrict__ src, int rows, i
         nv.y = h[3] | (static_cast<uint32_t>(h[4]) << 16);
         nv.z = h[5] | (static_cast<uint32_t>(h[6]) << 16);
         nv.w = h[7] | (static_cast<uint32_t>(h[8]) << 16);
-        *reinterpret_cast<uint4 *>(tile + (l * kTileRows + i) * 16) = nv;
-        *reinterpret_cast<uint16_t *>(tile + kTileNibBytes + (l * kTileRows + i) * 2) = h[0];
+        *reinterpret_cast<uint4 *>(tile + (i * kLanes + l) * 16) = nv;
+        *reinterpret_cast<uint16_t *>(tile + kTileNibBytes + (i * kLanes + l) * 2) = h[0];
     }
 }
 
 using TileKernelFn = void (*)(TileParams);
 
-template <int XMODE, int KS>
-TileKernelFn pick_cps(int cps) {
-    switch (cps) {
-        case 1: return q4_tile_kernel<XMODE, 1, KS>;
-        case 2: return q4_tile_kernel<XMODE, 2, KS>;
-        case 3: return q4_tile_kernel<XMODE, 3, KS>;
-        case 4: return q4_tile_kernel<XMODE, 4, KS>;
-        case 5: return q4_tile_kernel<XMODE, 5, KS>;
-        case 6: return q4_tile_kernel<XMODE, 6, KS>;
-        case 7: return q4_tile_kernel<XMODE, 7, KS>;
-        case 8: return q4_tile_kernel<XMODE, 8, KS>;
-        default: return nullptr;
-    }
-}
-
-template <int XMODE>
-TileKernelFn pick_tile(int cps, int ks) {
-    if (ks == 1) return pick_cps<XMODE, 1>(cps);
-    if (ks == 2) return pick_cps<XMODE, 2>(cps);
-    if (ks == 4) return pick_cps<XMODE, 4>(cps);
-    return nullptr;
+TileKernelFn pick_tile(int xmode, bool xreg) {
+    if (xmode == kXF32) return xreg ? q4_tile_kernel<kXF32, true> : q4_tile_kernel<kXF32, false>;
+    return xreg ? q4_tile_kernel<kXPacked, true> : q4_tile_kernel<kXPacked, false>;
 }
 
 struct TilePlan {
@@ -510,14 +520,8 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
     const char *why = nullptr;
     if (int rc = tile_validate(L, &why)) return rc;
     const int nb = L.k / kQK, nch = nb / kLanes;
-    // K-slices: enough that a slice has at most 8 chunks, more if asked.
-    int ks = 1;
-    while (ks < 4 && (ks * kMaxCps < nch || ks < tu.kslices)) ks *= 2;
-    while (ks > 1 && ks > nch) ks /= 2;  // every slice gets at least one chunk
-    const int cps = (nch + ks - 1) / ks;
-    if (cps > kMaxCps) return kErrInval;
-    TileKernelFn fn = L.xmode == kXF32 ? pick_tile<kXF32>(cps, ks) : pick_tile<kXPacked>(cps, ks);
-    if (!fn) return kErrInval;
+    if (nb > kConsumers) return kErrInval;  // x staging: one consumer thread per block
+    TileKernelFn fn = pick_tile(L.xmode, nch <= kXregChunks);
     TileParams p{};
     p.w = L.w;
     p.y = L.y;
@@ -530,7 +534,6 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
     p.nch = nch;
     p.groups = (L.rows + kTileRows - 1) / kTileRows;
     p.slot_bytes = nch * kTileBytes;
-    p.stages = tu.stages < 1 ? 1 : (tu.stages > kMaxStages ? kMaxStages : tu.stages);
     p.round_mode = L.round_mode;
     p.l2_policy = L.l2_policy;
     if (L.sel_out) {
@@ -541,18 +544,19 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
         p.sel_ticket = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(L.sel_scratch) + kSelMaxCtas * sizeof(float2));
     }
     p.dec = L.dec;
-    const int threads = kTileThreads * ks;
-    if (L.dec.pro != kProPlain && nb > threads) return kErrInval;  // one thread per x block
     const int xarea = xarea_bytes(L.k) + (L.dec.pro != kProPlain ? norm_extra_bytes(L.k) : 0);
-    const int fixed = kSmemAlign + kBarBytes + kRedBytes + (ks > 1 ? nch * kTileThreads * 4 : 0) + xarea;
-    const int limit = max_smem_optin();
-    while (p.stages > 1 && fixed + p.stages * p.slot_bytes > limit) p.stages -= 1;
-    const int smem = fixed + p.stages * p.slot_bytes;
+    const int fixed = kSmemAlign + xarea;
+    const int limit = max_smem_optin() - 1024;  // static shared memory
+    int stages = tu.stages < 1 ? 1 : (tu.stages > kMaxStages ? kMaxStages : tu.stages);
+    while (stages > 1 && fixed + stages * p.slot_bytes > limit) stages -= 1;
+    p.stages = stages;
+    const int smem = fixed + stages * p.slot_bytes;
     if (smem > limit) return kErrInval;
     const int sms = sm_count();
     if (sms <= 0) return kErrNoDev;
     int per_sm = tu.ctas_per_sm < 1 ? 1 : tu.ctas_per_sm;
-    const int fit = resident_ctas(reinterpret_cast<const void *>(fn), threads, smem);
+    const int fit = resident_ctas(reinterpret_cast<const void *>(fn), kTileThreads, smem);
+    if (fit < 1) return kErrInval;
     if (per_sm > fit) per_sm = fit;  // one wave: every CTA resident at once
     int grid = sms * per_sm;
     if (grid > p.groups) grid = p.groups;
@@ -561,7 +565,7 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
     out->fn = fn;
     out->grid = grid;
     out->smem = smem;
-    out->threads = threads;
+    out->threads = kTileThreads;
     return 0;
 }
 

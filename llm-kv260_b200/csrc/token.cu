@@ -364,10 +364,12 @@ __device__ void write_embedding(const TokenArgs &a, int k, int tok) {
 
 // ------------------------------------------------------------------ GEMV phase
 
-// Block term of chunk-tile `tile` for thread u = lane * 16 + row (q4tile.cu).
+// Block term of chunk-tile `tile` for thread u = lane * 16 + row; the tile
+// holds row i, lane l at (i * 8 + l) (q4tile.cu).
 __device__ __forceinline__ float mk_term(const uint8_t *tile, int u, const XBlock &xb) {
-    const uint4 nv = *reinterpret_cast<const uint4 *>(tile + u * 16);
-    const uint32_t db = *reinterpret_cast<const uint16_t *>(tile + kTileRows * kLanes * 16 + u * 2);
+    const int v = (u % kTileRows) * kLanes + u / kTileRows;
+    const uint4 nv = *reinterpret_cast<const uint4 *>(tile + v * 16);
+    const uint32_t db = *reinterpret_cast<const uint16_t *>(tile + kTileRows * kLanes * 16 + v * 2);
     const uint32_t n[4] = {nv.x, nv.y, nv.z, nv.w};
     return block_term_words(n, db, xb);
 }

@@ -46,6 +46,7 @@ def main() -> None:
     ap.add_argument("--launches", type=int, default=12)
     ap.add_argument("--pick", type=int, default=0)
     ap.add_argument("--device", type=int, default=0)
+    ap.add_argument("--stages", type=int, default=8, help="shared-memory ring stages per CTA")
     args = ap.parse_args()
     if args.rows * args.k * 18 // 32 * args.mats > 4 << 30:
         raise SystemExit("profile case larger than 4 GB; keep profiler captures small")
@@ -58,7 +59,7 @@ def main() -> None:
     eng = pkg.Engine(args.device, stream=0)
     stream = torch.cuda.Stream(args.device)
     eng.set_stream(stream.cuda_stream)
-    eng.configure(fuse_quantize=1, pdl=1, stages=4, ctas_per_sm=4, kslices=1)
+    eng.configure(fuse_quantize=1, pdl=1, stages=args.stages, ctas_per_sm=4, kslices=1)
     mats = []
     for i in range(args.mats):
         t = torch.from_numpy(synth_q4_0(args.rows, args.k, 9000 + i)).to(dev)

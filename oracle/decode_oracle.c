@@ -252,7 +252,7 @@ int odec_create(odec_t **out, const odec_config_t *cfg, const odec_layer_t *laye
     *out = NULL;
     const odec_config_t c = *cfg;
     const int n = c.nranks;
-    if (n < 1 || c.n_layer < 1 || c.head_dim % 16 || c.n_embd % 256 || c.n_ff % 256 || c.n_head % c.n_head_kv ||
+    if (n < 1 || n > 8 || c.n_layer < 1 || c.head_dim % 16 || c.n_embd % 256 || c.n_ff % 256 || c.n_head % c.n_head_kv ||
         c.n_head % n || c.n_head_kv % n || c.n_vocab % n || c.ctx_max < 1 || c.n_embd != c.n_head * c.head_dim)
         return -1;
     odec_t *d = calloc(1, sizeof(odec_t));
@@ -364,8 +364,8 @@ static void allreduce_add(odec_t *d) {
 static void pick(const odec_t *d, int *tok, float *val) {
     enum { K = 40 };
     const int n = d->c.nranks;
-    float av[8 * K];
-    int ai[8 * K];
+    float av[8 * K] = {0.0f};
+    int ai[8 * K] = {0};
     int na = 0;
     for (int r = 0; r < n; ++r) {
         float mv[K];

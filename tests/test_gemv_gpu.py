@@ -266,7 +266,7 @@ def test_udmabuf_pool_clean_run_invalidate(torch_mod, pkg, oracle):
 
 
 def test_repack_layout_matches_its_definition(torch_mod, pkg, eng, oracle):
-    """Tile (g, c) at ((g*nch)+c)*2304: nibbles [lane][row][16], then scales [lane][row]; padded rows zero."""
+    """Tile (g, c) at ((g*nch)+c)*2304: nibbles [row][lane][16], then scales [row][lane]; padded rows zero."""
     torch = torch_mod
     rows, k = 37, 512
     blocks = oracle.quantize_q4_0(cases.std_weights(rows, k, 81))
@@ -279,8 +279,8 @@ def test_repack_layout_matches_its_definition(torch_mod, pkg, eng, oracle):
         for b in range(nb):
             g, i, c, l = r // 16, r % 16, b // 8, b % 8
             base = (g * nch + c) * 2304
-            nib = tiles[base + (l * 16 + i) * 16: base + (l * 16 + i) * 16 + 16]
-            sc = tiles[base + 2048 + (l * 16 + i) * 2: base + 2048 + (l * 16 + i) * 2 + 2]
+            nib = tiles[base + (i * 8 + l) * 16: base + (i * 8 + l) * 16 + 16]
+            sc = tiles[base + 2048 + (i * 8 + l) * 2: base + 2048 + (i * 8 + l) * 2 + 2]
             if r < rows:
                 assert np.array_equal(nib, blocks[r, b * 18 + 2:b * 18 + 18])
                 assert np.array_equal(sc, blocks[r, b * 18:b * 18 + 2])
