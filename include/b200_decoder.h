@@ -113,8 +113,15 @@ B200_API int b200_decoder_read(b200_decoder_t *d, int what, void *host, uint64_t
  * device global timer in ns: 0 phase start (its barrier passed), 1 x staged,
  * 2 warpgroup 0's rows done, 3 phase end, 4 and 5 the time warpgroups 0 and 1
  * waited for weight stages, 6 warpgroup 1's rows done, 7 unused -- read back
- * as buffer 7 (uint64[tokens][phases][SMs][8]). 0 turns it off. A B200
- * extension with no reference counterpart. */
+ * as buffer 7 (uint64[tokens][phases][SMs][8]).
+ * Graph mode (tokens 0 or 1): every token run records its 5 * n_layer + 1
+ * kernel launches (per layer q|k|v, attention, o, gate|up, down; then
+ * lm_head), overwriting the previous token's -- per (launch, CTA < 1024)
+ * eight stamps: 0 CTA set up, 1 the previous kernel's results visible, 2
+ * input staged (attention: softmax done), 3 CTA end, and for attention 4 q
+ * staged, 5 scores, 6 maxima, 7 exponentials done; read back as buffer 7
+ * (uint64[launches][1024][8], zero where a launch has no such CTA or stamp).
+ * 0 turns tracing off. A B200 extension with no reference counterpart. */
 B200_API int b200_decoder_trace(b200_decoder_t *d, int tokens);
 
 /* Device status: bit 1 a weight copy wait ran out, bit 2 a peer wait ran

@@ -48,6 +48,16 @@ __device__ __forceinline__ float rope_pair(float x0, float x1, float c, float s,
     return even ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s)) : __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
 }
 
+// Where element e (0 <= e < hd) of the K row of position `pos` sits inside
+// that row in the K cache: the row's 16-byte segments are XOR-swizzled by
+// the position (segment s stored at (s & ~7) | ((s & 7) ^ (pos & 7))), so the
+// attention's threads, one row each, read 8 consecutive rows' segment s from
+// 8 different shared-memory bank groups. esz: 2 (float16) or 4 (float32).
+__host__ __device__ __forceinline__ int k_swizzled(int e, int pos, int esz) {
+    const int per = 16 / esz, s = e / per;
+    return ((s & ~7) | ((s & 7) ^ (pos & 7))) * per + e % per;
+}
+
 // RMSNorm's sum of squares, tp_llama.cpp:557-564: the reference sums
 // x[i]^2 in double in four lanes (i mod 4), sequentially, then
 // (l0 + l2) + (l1 + l3), and uses (float)(ss / n). A parallel sum in another

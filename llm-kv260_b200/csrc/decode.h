@@ -13,20 +13,23 @@ namespace b200 {
 
 struct AttnLaunch {
     const float *q = nullptr;       // this rank's roped q rows: [heads_local][head_dim]
-    const void *kcache = nullptr;   // this layer's caches: [kv head][ctx_max][head_dim]
-    const void *vcache = nullptr;
+    const void *kcache = nullptr;   // this layer's K cache [kv head][kv_stride][head_dim]
+    const void *vcache = nullptr;   // and V^T cache [kv head][head_dim][kv_stride] (attn_core.cuh)
     float *out = nullptr;           // [heads_local][head_dim]
     const int *pos = nullptr;       // current position (device)
     int head_dim = 0;               // 64 or 128
     int group = 0;                  // query heads per KV head, 1..4
     int kvh_local = 0;              // KV heads on this rank (one CTA each)
     int ctx_max = 0;
+    int kv_stride = 0;              // attn_kv_stride(ctx_max): positions per head in the caches
     int kv_f16 = 1;
     float scale = 0.0f;             // 1 / sqrtf(head_dim)
     bool pdl = true;
+    uint64_t *trace = nullptr;      // optional launch trace (q4gemv.h, kTraceCtas); stamp 2 = softmax done
 };
 
-int attn_smem_bytes(int head_dim, int group, int ctx_max);
+int attn_kv_stride(int ctx_max);  // ctx_max rounded up to a multiple of 8
+int attn_smem_bytes(int head_dim, int kv_f16, int ctx_max);
 int attn_launch(const AttnLaunch &L, cudaStream_t stream);
 
 // ------------------------------------------------------- persistent token kernel
@@ -70,6 +73,7 @@ struct TokenArgs {
     const float *logits = nullptr;       // lm_head output (for the NaN-at-0 rule)
     const float *rope_cs = nullptr;
     int n_embd = 0, head_dim = 0, q_rows = 0, kv_rows = 0, ctx_max = 0, kv_f16 = 1, group = 0, kvh_local = 0;
+    int kv_stride = 0;                   // positions per head in the caches (attn_kv_stride)
     int vocab_base = 0;
     float scale = 0.0f, eps = 0.0f;
     int exact_norm = 0, round_mode = 0;

@@ -44,7 +44,8 @@ namespace {
 struct DecLayer {
     uint8_t *qkv = nullptr, *o = nullptr, *gateup = nullptr, *down = nullptr;  // tiles
     float *attn_norm = nullptr, *ffn_norm = nullptr;
-    uint8_t *kcache = nullptr, *vcache = nullptr;  // [kv head][ctx_max][head_dim]
+    uint8_t *kcache = nullptr;  // K   [kv head][kv_stride][head_dim]
+    uint8_t *vcache = nullptr;  // V^T [kv head][head_dim][kv_stride] (attn_core.cuh)
     bool set = false;
 };
 
@@ -107,8 +108,9 @@ struct b200_decoder {
     int *abort_flag;
     float2 *cand;
     int *host_tokens_dev;         // host_io + 2 as a device address
-    uint64_t *trace;              // optional phase trace (b200_decoder_trace)
+    uint64_t *trace;              // optional trace (b200_decoder_trace): persistent phases, or graph launches
     int trace_tokens;
+    int trace_launches;           // graph mode: launches with a trace record (5 per layer + lm_head)
     // exchange
     uint64_t *win_words[kMaxDecodeRanks];
     uint64_t slot_words;
@@ -211,6 +213,11 @@ void residual_epilogue(const b200_decoder_t *d, TileLaunch &L, int ar_index) {
     L.dec.peer_status = d->peer_status;
 }
 
+// Graph mode's launch trace: record `i` of the token's launches, or none.
+uint64_t *launch_trace(const b200_decoder_t *d, int i) {
+    return (d->trace && !d->persistent) ? d->trace + static_cast<size_t>(i) * kTraceCtas * kTraceStamps : nullptr;
+}
+
 int launch(const b200_decoder_t *d, const TileLaunch &L, const char *what) {
     const char *why = nullptr;
     if (tile_validate(L, &why)) return dfail(kErrInval, "decoder: %s GEMV: %s", what, why);
@@ -233,9 +240,11 @@ int enqueue_token(b200_decoder_t *d) {
         A.dec.q_rows = d->q_rows;
         A.dec.kv_rows = d->kv_rows;
         A.dec.ctx_max = c.ctx_max;
+        A.dec.kv_stride = attn_kv_stride(c.ctx_max);
         A.dec.kv_f16 = c.kv_f16;
         A.dec.kcache = W.kcache;
         A.dec.vcache = W.vcache;
+        A.trace = launch_trace(d, 5 * l);
         if (int rc = launch(d, A, "q|k|v")) return rc;
 
         AttnLaunch T;
@@ -248,23 +257,28 @@ int enqueue_token(b200_decoder_t *d) {
         T.group = d->group;
         T.kvh_local = d->kvh_local;
         T.ctx_max = c.ctx_max;
+        T.kv_stride = attn_kv_stride(c.ctx_max);
         T.kv_f16 = c.kv_f16;
         T.scale = 1.0f / sqrtf(static_cast<float>(c.head_dim));
+        T.trace = launch_trace(d, 5 * l + 1);
         if (int rc = attn_launch(T, d->stream))
             return dfail(rc, "decoder: attention launch failed: %s", cudaGetErrorString(cudaGetLastError()));
 
         TileLaunch O = gemv_base(d, W.o, e, d->o_k, d->attn, nullptr);
         residual_epilogue(d, O, 2 * l);
+        O.trace = launch_trace(d, 5 * l + 2);
         if (int rc = launch(d, O, "o")) return rc;
 
         TileLaunch G = gemv_base(d, W.gateup, 2 * d->ff_rows, e, d->res, nullptr);
         norm_prologue(d, G, kProRmsnorm, W.ffn_norm);
         G.dec.epi = kEpiSiluPairs;
         G.dec.act = d->act;
+        G.trace = launch_trace(d, 5 * l + 3);
         if (int rc = launch(d, G, "gate|up")) return rc;
 
         TileLaunch D = gemv_base(d, W.down, e, d->down_k, d->act, nullptr);
         residual_epilogue(d, D, 2 * l + 1);
+        D.trace = launch_trace(d, 5 * l + 4);
         if (int rc = launch(d, D, "down")) return rc;
     }
     TileLaunch H = gemv_base(d, d->lm_head, d->vocab_rows, e, d->res, d->logits);
@@ -279,6 +293,7 @@ int enqueue_token(b200_decoder_t *d) {
         H.dec.n_prompt = &d->st->n_prompt;
         H.dec.ctx_max = c.ctx_max;
     }
+    H.trace = launch_trace(d, 5 * c.n_layer);
     if (int rc = launch(d, H, "lm_head")) return rc;
     if (d->nranks > 1) {
         if (int rc = b200_allgather_pick(d->comm, reinterpret_cast<uint64_t>(d->st->pick_local),
@@ -320,6 +335,7 @@ TokenArgs token_args(const b200_decoder_t *d, int ntokens) {
     a.q_rows = d->q_rows;
     a.kv_rows = d->kv_rows;
     a.ctx_max = c.ctx_max;
+    a.kv_stride = attn_kv_stride(c.ctx_max);
     a.kv_f16 = c.kv_f16;
     a.group = d->group;
     a.kvh_local = d->kvh_local;
@@ -538,6 +554,8 @@ extern "C" int b200_decoder_create(b200_decoder_t **out, const b200_decoder_conf
         return rc;
     };
     if (int rc = use_dev(d)) return bail(rc);
+    if (!c.persistent && attn_smem_bytes(c.head_dim, c.kv_f16, c.ctx_max) > max_smem_optin())
+        return bail(dfail(kErrInval, "decoder: attention over ctx_max %d positions does not fit shared memory", c.ctx_max));
     if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess)
         return bail(dfail(kErrCuda, "decoder: stream creation failed"));
     if (nranks > 1) {
@@ -548,7 +566,7 @@ extern "C" int b200_decoder_create(b200_decoder_t **out, const b200_decoder_conf
             return bail(dfail(kErrInval, "decoder: the communicator was created for fewer than n_embd floats"));
     }
     const int e = c.n_embd;
-    const size_t kv_elems = static_cast<size_t>(c.n_layer) * d->kvh_local * c.ctx_max * c.head_dim;
+    const size_t kv_elems = static_cast<size_t>(c.n_layer) * d->kvh_local * attn_kv_stride(c.ctx_max) * c.head_dim;
     const size_t kv_bytes = kv_elems * (c.kv_f16 ? 2 : 4);
     int rc = 0;
     if (!rc) rc = dalloc(d, &d->res, 4 * static_cast<size_t>(e));
@@ -594,7 +612,7 @@ extern "C" int b200_decoder_create(b200_decoder_t **out, const b200_decoder_conf
     for (int p = 0; p < c.ctx_max; ++p) b200_rope_table(cs.data() + static_cast<size_t>(p) * c.head_dim, c.head_dim, p, c.rope_base);
     if (int r2 = h2d(d->rope_cs, cs.data(), cs.size() * 4, d->stream)) return bail(r2);
     if (cudaStreamSynchronize(d->stream) != cudaSuccess) return bail(dfail(kErrCuda, "decoder: initialisation failed"));
-    const size_t per_layer = static_cast<size_t>(d->kvh_local) * c.ctx_max * c.head_dim * (c.kv_f16 ? 2 : 4);
+    const size_t per_layer = static_cast<size_t>(d->kvh_local) * attn_kv_stride(c.ctx_max) * c.head_dim * (c.kv_f16 ? 2 : 4);
     for (int l = 0; l < c.n_layer; ++l) {
         d->layers[l].kcache = d->kv + l * per_layer;
         d->layers[l].vcache = d->kv + kv_bytes + l * per_layer;
@@ -741,7 +759,29 @@ extern "C" int b200_decoder_generate(b200_decoder_t *d, const int32_t *prompt, i
 
 extern "C" int b200_decoder_trace(b200_decoder_t *d, int tokens) {
     if (!d || tokens < 0 || tokens > 64) return dfail(kErrInval, "decoder: trace 0..64 tokens");
-    if (!d->persistent) return dfail(kErrInval, "decoder: the phase trace is the persistent kernel's");
+    if (!d->persistent) {
+        // graph mode: the launches of the last token run, recorded by every replay
+        if (tokens > 1) return dfail(kErrInval, "decoder: graph mode traces one token (the last one run)");
+        if (int rc = use_dev(d)) return rc;
+        if (cudaStreamSynchronize(d->stream) != cudaSuccess) return dfail(kErrCuda, "decoder: stream failed");
+        const int nl = 5 * d->c.n_layer + 1;
+        if (tokens && !d->trace_launches) {
+            const size_t bytes = static_cast<size_t>(nl) * kTraceCtas * kTraceStamps * 8;
+            if (int rc = dalloc(d, &d->trace, bytes)) return rc;
+            if (cudaMemset(d->trace, 0, bytes) != cudaSuccess) return dfail(kErrCuda, "decoder: trace reset failed");
+            d->trace_launches = nl;
+        }
+        if (tokens != d->trace_tokens && d->graph) {  // recapture with (or without) the trace pointers
+            cudaGraphExecDestroy(d->graph);
+            d->graph = nullptr;
+        }
+        d->trace_tokens = tokens;
+        if (!tokens) {
+            d->trace = nullptr;
+            d->trace_launches = 0;
+        }
+        return 0;
+    }
     if (int rc = ready(d)) return rc;
     if (tokens > d->trace_tokens) {
         const int sms = sm_count();
@@ -765,7 +805,11 @@ extern "C" int b200_decoder_read(b200_decoder_t *d, int what, void *host, uint64
         case 4: src = d->qkv_y; n = 4ull * (d->q_rows + 2 * d->kv_rows); break;
         case 5: src = d->attn; n = 4ull * d->o_k; break;
         case 6: src = d->act; n = 4ull * d->down_k; break;
-        case 7: src = d->trace; n = 8ull * d->trace_tokens * d->nphases * sm_count() * 8; break;
+        case 7:
+            src = d->trace;
+            n = d->persistent ? 8ull * d->trace_tokens * d->nphases * sm_count() * 8
+                              : 8ull * d->trace_launches * kTraceCtas * kTraceStamps;
+            break;
         default: return dfail(kErrInval, "decoder: unknown buffer %d", what);
     }
     if (bytes != n) return dfail(kErrInval, "decoder: buffer %d holds %llu bytes", what, static_cast<unsigned long long>(n));

@@ -97,6 +97,18 @@ __device__ __forceinline__ uint64_t l2_policy_evict_normal() {
     return p;
 }
 
+// 16-byte asynchronous global -> shared copy through L2 only (no L1), in the
+// thread's current group; groups complete in commit order.
+__device__ __forceinline__ void cp_async16(void *dst_smem, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's committed groups are still pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Programmatic dependent launch: both are no-ops when the grid was not
 // launched with the programmatic-serialization attribute.
 __device__ __forceinline__ void pdl_wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

@@ -102,6 +102,15 @@ enum Epilogue : int {
 
 constexpr int kMaxDecodeRanks = 8;
 
+// Optional launch trace of the decoder's per-op kernels: thread 0 of CTA b
+// (b < kTraceCtas) writes global-timer stamps (ns) at trace[b * 8 + j]:
+// 0 after the CTA's set-up, 1 when the previous kernel's results are visible
+// (griddepcontrol.wait returned), 2 when its input is staged (attention: the
+// softmax done), 3 at its end; attention also 4 q staged, 5 scores done,
+// 6 maxima done, 7 exponentials done.
+constexpr int kTraceCtas = 1024;
+constexpr int kTraceStamps = 8;
+
 struct DecodeOps {
     int pro = kProPlain;
     int epi = kEpiStore;
@@ -114,8 +123,9 @@ struct DecodeOps {
     const int *pos = nullptr;          // the current position (device)
     const float *rope_cs = nullptr;    // [ctx_max][head_dim]: cos, sin of pair i at 2i, 2i+1
     int head_dim = 0, q_rows = 0, kv_rows = 0, ctx_max = 0, kv_f16 = 1;
-    void *kcache = nullptr;            // this layer's caches, [kv head][ctx_max][head_dim]
-    void *vcache = nullptr;
+    int kv_stride = 0;                 // positions per head in the caches (a multiple of 8, >= ctx_max)
+    void *kcache = nullptr;            // this layer's K cache [kv head][kv_stride][head_dim]
+    void *vcache = nullptr;            // and V^T cache [kv head][head_dim][kv_stride]
     float *act = nullptr;              // kEpiSiluPairs output [rows / 2]
     int nranks = 1, rank = 0;          // kEpiResidual across ranks:
     uint64_t *win_words[kMaxDecodeRanks] = {};  // every rank's word area as mapped here, [slot][source rank][row]
@@ -144,6 +154,7 @@ struct TileLaunch {
     int sel_base = 0;
     void *sel_scratch = nullptr;  // tile_select_scratch_bytes(), ticket zeroed once
     DecodeOps dec;                // decoder prologue/epilogue (plain GEMV by default)
+    uint64_t *trace = nullptr;    // optional: [CTA < kTraceCtas][4] global-timer stamps (kTraceStamps)
 };
 int tile_select_scratch_bytes();
 

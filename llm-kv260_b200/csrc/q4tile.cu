@@ -63,7 +63,12 @@ struct TileParams {
     float2 *sel_cand;    // gridDim.x entries: (value, row as float bits)
     unsigned *sel_ticket;
     DecodeOps dec;       // decoder prologue / epilogue (q4gemv.h)
+    uint64_t *trace;     // optional launch trace (q4gemv.h, kTraceCtas)
 };
+
+__device__ __forceinline__ void trace_stamp(uint64_t *trace, int j) {
+    if (trace && threadIdx.x == 0 && blockIdx.x < kTraceCtas) trace[blockIdx.x * kTraceStamps + j] = globaltimer_ns();
+}
 
 constexpr uint64_t kPeerTimeoutNs = 1000000000ull;  // a peer's row words: 1 s
 
@@ -77,102 +82,140 @@ __device__ __forceinline__ uint64_t ld_word(const uint64_t *p) {
     return w;
 }
 
-// Decoder prologue: x = rmsnorm(res) * norm_w, quantised into xs (the same
-// layout as stage_x). One thread per 32-block. res is the residual stream,
-// or (kProEmbedNorm) the token's embedding row, which CTA 0 also writes to
-// res. The sum of squares runs in parallel in double; rms_float_is_safe
-// decides whether its float is the reference's, else threads 0-3 redo the
-// four lane sums in the reference's order from the copy of x in xf.
-__device__ __noinline__ void stage_x_norm(const TileParams &p, uint8_t *xs, float *xf, double *dred) {
-    __shared__ float s_f;
-    __shared__ int s_exact;
-    const int k = p.k, nb = k / kQK, b = threadIdx.x, lane = threadIdx.x % 32, warp = threadIdx.x / 32;
-    float v[32];
-    double ss = 0.0;
-    if (b < nb) {
-        if (p.dec.pro == kProEmbedNorm) {
+// Threads per 32-block when staging a float32 x: 4, 2 or 1, as many as the
+// consumers allow for k/32 blocks.
+__device__ __forceinline__ int stage_tpb(int nb) { return nb * 4 <= kConsumers ? 4 : (nb * 2 <= kConsumers ? 2 : 1); }
+
+// Consumer side of staging a float32 x into xs (int8[k], then (float32 d,
+// int32 sum) per block -- stage_x's layout), TPB threads per 32-block with
+// E = 32 / TPB consecutive values each. The prologue's x is the plain input,
+// or rmsnorm(res) * norm_w (tp_llama.cpp:557-569), or that of the token's
+// embedding row (593-604), which CTA 0 also writes to res. The norm weights
+// do not depend on the previous kernel, so they load before this waits for
+// it. The sum of squares runs in parallel in double (each square is exact)
+// and every thread combines the warp sums in the same order, so all take
+// the same decision: rms_float_is_safe, else threads 0-3 redo the
+// reference's four sequential lane sums from the copy of x in xf. The
+// block's Q8_0 quantisation (q4_0.py:83-97) meets its maximum and its int
+// sum across the block's TPB adjacent lanes by xor shuffles: the maximum
+// (fmaxf) and an integer sum do not depend on the order.
+template <int TPB>
+__device__ __forceinline__ void stage_x_f32(const TileParams &p, uint8_t *xs, float *xf, double *dred) {
+    constexpr int E = 32 / TPB;
+    const int k = p.k, nb = k / kQK, t = threadIdx.x, b = t / TPB, r = t % TPB, lane = t % 32, warp = t / 32;
+    const bool live = b < nb;
+    const int i0 = 32 * b + E * r;
+    const int pro = p.dec.pro;
+    float w[E];
+    if (pro != kProPlain && live) {
+        const float4 *wv = reinterpret_cast<const float4 *>(p.dec.norm_w + i0);
+#pragma unroll
+        for (int j = 0; j < E / 4; ++j) {
+            const float4 f = __ldg(wv + j);
+            w[4 * j] = f.x;
+            w[4 * j + 1] = f.y;
+            w[4 * j + 2] = f.z;
+            w[4 * j + 3] = f.w;
+        }
+    }
+    pdl_wait_prior_grid();
+    trace_stamp(p.trace, 1);
+    float v[E];
+#pragma unroll
+    for (int j = 0; j < E; ++j) v[j] = 0.0f;
+    if (live) {
+        if (pro == kProEmbedNorm) {
             const int tok = p.dec.tokens[*p.dec.pos];
-            const uint16_t *blk =
-                reinterpret_cast<const uint16_t *>(p.dec.embd + (static_cast<size_t>(tok) * nb + b) * kBlockBytes);
-            uint16_t h[9];
+            const uint8_t *blk = p.dec.embd + (static_cast<size_t>(tok) * nb + b) * kBlockBytes;
+            const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(blk)));
 #pragma unroll
-            for (int j = 0; j < 9; ++j) h[j] = blk[j];
-            const float d = __half2float(__ushort_as_half(h[0]));
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int byte = (h[1 + j / 2] >> (8 * (j & 1))) & 0xff;
-                v[j] = __fmul_rn(__int2float_rn((byte & 0xF) - 8), d);
-                v[j + 16] = __fmul_rn(__int2float_rn((byte >> 4) - 8), d);
+            for (int j = 0; j < E; ++j) {
+                const int i = E * r + j;  // weight i of the block: low nibble of byte i, or high of byte i - 16
+                const int byte = blk[2 + (i & 15)];
+                const int nib = i < 16 ? (byte & 0xF) : (byte >> 4);
+                v[j] = __fmul_rn(__int2float_rn(nib - 8), d);
             }
             if (blockIdx.x == 0) {
-                float4 *dst = reinterpret_cast<float4 *>(p.dec.res) + 8 * b;
+                float4 *dst = reinterpret_cast<float4 *>(p.dec.res + i0);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                for (int j = 0; j < E / 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             }
         } else {
-            const float4 *src = reinterpret_cast<const float4 *>(p.dec.res) + 8 * b;
+            const float4 *src = reinterpret_cast<const float4 *>((pro == kProPlain ? static_cast<const float *>(p.x) : p.dec.res) + i0);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float4 f = src[j];
+            for (int j = 0; j < E / 4; ++j) {
+                const float4 f = __ldcg(src + j);
                 v[4 * j] = f.x;
                 v[4 * j + 1] = f.y;
                 v[4 * j + 2] = f.z;
                 v[4 * j + 3] = f.w;
             }
         }
-#pragma unroll
-        for (int j = 0; j < 32; ++j) ss = __dadd_rn(ss, __dmul_rn(static_cast<double>(v[j]), static_cast<double>(v[j])));
-        float4 *xd = reinterpret_cast<float4 *>(xf) + 8 * b;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) xd[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
     }
+    if (pro != kProPlain) {
+        double ss = 0.0;
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(kFullMask, ss, off));
-    if (lane == 0) dred[warp] = ss;
-    named_sync(1, kConsumers);
-    if (threadIdx.x == 0) {
+        for (int j = 0; j < E; ++j) ss = __dadd_rn(ss, __dmul_rn(static_cast<double>(v[j]), static_cast<double>(v[j])));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(kFullMask, ss, off));
+        if (lane == 0) dred[warp] = ss;
+        if (live) {
+            float4 *xd = reinterpret_cast<float4 *>(xf + i0);
+#pragma unroll
+            for (int j = 0; j < E / 4; ++j) xd[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+        named_sync(1, kConsumers);
         double tot = 0.0;
-        for (int w = 0; w < kConsumers / 32; ++w) tot = __dadd_rn(tot, dred[w]);
-        const double q = __ddiv_rn(tot, static_cast<double>(k));
-        const float f = __double2float_rn(q);
-        s_exact = p.dec.exact_norm || !rms_float_is_safe(q, f, k);
-        s_f = f;
-    }
-    named_sync(1, kConsumers);
-    if (s_exact) {
-        // tp_llama.cpp:560-564: lane j sums x[i]^2 for i = j, j+4, ... in order
-        if (threadIdx.x < 4) {
-            double a = 0.0;
-            for (int i = threadIdx.x; i < k; i += 4)
-                a = __dadd_rn(a, __dmul_rn(static_cast<double>(xf[i]), static_cast<double>(xf[i])));
-            dred[threadIdx.x] = a;
-        }
-        named_sync(1, kConsumers);
-        if (threadIdx.x == 0) {
-            const double ss2 = __dadd_rn(__dadd_rn(dred[0], dred[2]), __dadd_rn(dred[1], dred[3]));
-            s_f = __double2float_rn(__ddiv_rn(ss2, static_cast<double>(k)));
-        }
-        named_sync(1, kConsumers);
-    }
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(s_f, p.dec.eps)));
-    if (b < nb) {
-        const float4 *wv = reinterpret_cast<const float4 *>(p.dec.norm_w) + 8 * b;
-        float4 hv[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float4 w4 = __ldg(wv + j);
-            hv[j].x = __fmul_rn(__fmul_rn(v[4 * j], scale), w4.x);
-            hv[j].y = __fmul_rn(__fmul_rn(v[4 * j + 1], scale), w4.y);
-            hv[j].z = __fmul_rn(__fmul_rn(v[4 * j + 2], scale), w4.z);
-            hv[j].w = __fmul_rn(__fmul_rn(v[4 * j + 3], scale), w4.w);
+        for (int w8 = 0; w8 < kConsumers / 32; ++w8) tot = __dadd_rn(tot, dred[w8]);
+        const double q = __ddiv_rn(tot, static_cast<double>(k));
+        float f = __double2float_rn(q);
+        if (p.dec.exact_norm || !rms_float_is_safe(q, f, k)) {
+            // tp_llama.cpp:560-564: lane j sums x[i]^2 for i = j, j+4, ... in order
+            if (t < 4) {
+                double a = 0.0;
+                for (int i = t; i < k; i += 4) a = __dadd_rn(a, __dmul_rn(static_cast<double>(xf[i]), static_cast<double>(xf[i])));
+                dred[8 + t] = a;
+            }
+            named_sync(1, kConsumers);
+            const double ss2 = __dadd_rn(__dadd_rn(dred[8], dred[10]), __dadd_rn(dred[9], dred[11]));
+            f = __double2float_rn(__ddiv_rn(ss2, static_cast<double>(k)));
         }
-        uint32_t q[8];
-        float d;
-        const int sum = q8_quant_block(hv, p.round_mode, q, &d);
-        uint4 *qdst = reinterpret_cast<uint4 *>(xs + 32 * b);
-        qdst[0] = make_uint4(q[0], q[1], q[2], q[3]);
-        qdst[1] = make_uint4(q[4], q[5], q[6], q[7]);
-        reinterpret_cast<int2 *>(xs + k)[b] = make_int2(__float_as_int(__half2float(__float2half_rn(d))), sum);
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(f, p.dec.eps)));
+#pragma unroll
+        for (int j = 0; j < E; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], scale), w[j]);
+    }
+    // Q8_0 of the block (q8_quant_block's arithmetic, split over TPB lanes)
+    float am = fabsf(v[0]);
+#pragma unroll
+    for (int j = 1; j < E; ++j) am = fmaxf(am, fabsf(v[j]));
+#pragma unroll
+    for (int off = 1; off < TPB; off <<= 1) am = fmaxf(am, __shfl_xor_sync(kFullMask, am, off));
+    const float db = __fdiv_rn(am, 127.0f);
+    const float inv = db == 0.0f ? 0.0f : __fdiv_rn(1.0f, db);
+    uint32_t qw[E / 4];
+    int sum = 0;
+#pragma unroll
+    for (int j = 0; j < E / 4; ++j) {
+        const int q0 = q8_round(__fmul_rn(v[4 * j], inv), p.round_mode);
+        const int q1 = q8_round(__fmul_rn(v[4 * j + 1], inv), p.round_mode);
+        const int q2 = q8_round(__fmul_rn(v[4 * j + 2], inv), p.round_mode);
+        const int q3 = q8_round(__fmul_rn(v[4 * j + 3], inv), p.round_mode);
+        sum += q0 + q1 + q2 + q3;
+        qw[j] = (static_cast<uint32_t>(q0) & 0xffu) | ((static_cast<uint32_t>(q1) & 0xffu) << 8) |
+                ((static_cast<uint32_t>(q2) & 0xffu) << 16) | ((static_cast<uint32_t>(q3) & 0xffu) << 24);
+    }
+#pragma unroll
+    for (int off = 1; off < TPB; off <<= 1) sum += __shfl_xor_sync(kFullMask, sum, off);
+    if (live) {
+        if constexpr (E == 8) {
+            *reinterpret_cast<uint2 *>(xs + i0) = make_uint2(qw[0], qw[1]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < E / 16; ++j)
+                reinterpret_cast<uint4 *>(xs + i0)[j] = make_uint4(qw[4 * j], qw[4 * j + 1], qw[4 * j + 2], qw[4 * j + 3]);
+        }
+        if (r == 0) reinterpret_cast<int2 *>(xs + k)[b] = make_int2(__float_as_int(__half2float(__float2half_rn(db))), sum);
     }
 }
 
@@ -242,6 +285,7 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
     }
     __syncthreads();
     pdl_launch_dependents();
+    trace_stamp(p.trace, 0);
 
     if (warp == kConsumers / 32) {
         // producer: the weights do not depend on the previous kernel
@@ -268,13 +312,23 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
         return;
     }
 
-    pdl_wait_prior_grid();
-    if (XMODE == kXF32 && p.dec.pro != kProPlain)
-        stage_x_norm(p, xs, reinterpret_cast<float *>(xs + xarea_bytes(p.k)),
-                     reinterpret_cast<double *>(xs + xarea_bytes(p.k) + 4 * p.k));
-    else
+    if constexpr (XMODE == kXF32) {
+        float *xf = reinterpret_cast<float *>(xs + xarea_bytes(p.k));    // with a norm prologue only
+        double *dred = reinterpret_cast<double *>(xs + xarea_bytes(p.k) + 4 * p.k);
+        const int tpb = stage_tpb(p.nb);
+        if (tpb == 4)
+            stage_x_f32<4>(p, xs, xf, dred);
+        else if (tpb == 2)
+            stage_x_f32<2>(p, xs, xf, dred);
+        else
+            stage_x_f32<1>(p, xs, xf, dred);
+    } else {
+        pdl_wait_prior_grid();
+        trace_stamp(p.trace, 1);
         stage_x<XMODE>(p.x, p.k, p.round_mode, xs);
+    }
     named_sync(1, kConsumers);
+    trace_stamp(p.trace, 2);
 
     const int quad = warp / 4, i = (warp % 4) * 4 + (lane >> 3), l = lane & 7;
     XBlock xr[XREG ? kXregChunks : 1];
@@ -347,9 +401,13 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
                 }
                 p.y[row] = out;
                 if (row >= k0) {
+                    // K rows [kv head][stride][hd], segments swizzled by position
+                    // (k_swizzled); V transposed, [kv head][hd][stride]
                     const bool isk = row < v0;
-                    const int rr = row - (isk ? k0 : v0);
-                    const size_t at = (static_cast<size_t>(rr / hd) * p.dec.ctx_max + dpos) * hd + rr % hd;
+                    const int rr = row - (isk ? k0 : v0), st = p.dec.kv_stride;
+                    const size_t at =
+                        isk ? (static_cast<size_t>(rr / hd) * st + dpos) * hd + k_swizzled(rr % hd, dpos, p.dec.kv_f16 ? 2 : 4)
+                            : static_cast<size_t>(rr) * st + dpos;
                     void *cache = isk ? p.dec.kcache : p.dec.vcache;
                     if (p.dec.kv_f16)
                         static_cast<__half *>(cache)[at] = __float2half_rn(out);
@@ -474,6 +532,10 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
             }
         }
     }
+    if (p.trace) {
+        named_sync(1, kConsumers);
+        trace_stamp(p.trace, 3);
+    }
 }
 
 // GGUF rows -> tiles; one thread per (row, block), padded rows become zeros.
@@ -544,6 +606,7 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
         p.sel_ticket = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(L.sel_scratch) + kSelMaxCtas * sizeof(float2));
     }
     p.dec = L.dec;
+    p.trace = L.trace;
     const int xarea = xarea_bytes(L.k) + (L.dec.pro != kProPlain ? norm_extra_bytes(L.k) : 0);
     const int fixed = kSmemAlign + xarea;
     const int limit = max_smem_optin() - 1024;  // static shared memory
@@ -603,7 +666,7 @@ int tile_validate(const TileLaunch &L, const char **why) {
     if (D.epi == kEpiRopeKv) {
         if (!D.rope_cs || !D.kcache || !D.vcache || !D.pos || D.head_dim <= 0 || D.head_dim % 2 || D.q_rows % D.head_dim ||
             D.kv_rows % D.head_dim || D.q_rows % kTileRows || D.kv_rows % kTileRows || D.ctx_max <= 0 ||
-            L.rows != D.q_rows + 2 * D.kv_rows)
+            D.kv_stride < D.ctx_max || D.kv_stride % 8 || L.rows != D.q_rows + 2 * D.kv_rows)
             return bad("rope/KV epilogue: inconsistent q/k/v rows, head_dim or caches");
     }
     if (D.epi == kEpiSiluPairs && (!D.act || L.rows % 2)) return bad("silu epilogue: act needed, rows even");

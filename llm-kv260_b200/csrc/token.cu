@@ -38,6 +38,7 @@
 
 #include <cmath>
 
+#include "attn_core.cuh"
 #include "common.cuh"
 #include "decode.cuh"
 #include "decode.h"
@@ -50,13 +51,12 @@ constexpr int kStage = 8 * kTileBytes;  // 18432: 8 chunks of one 16-row group
 constexpr int kMaxRing = 16;
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr uint64_t kPeerWaitNs = 1000000000ull;
-constexpr int kAttnChunk = 16384;  // V bytes per attention chunk
 constexpr int kMaxBatch = 4;       // row groups a warpgroup runs side by side
 
 struct MkParams {
     TokenArgs a;
     int ring;  // stages in the ring
-    int off_xs, off_xf, off_dred, off_red, off_best, off_attn, off_sc;
+    int off_xs, off_xf, off_dred, off_red, off_best, off_attn;
 };
 
 // ------------------------------------------------------------------ waits
@@ -519,9 +519,13 @@ __device__ void gemv_phase(const MkParams &p, const TokenPhase &ph, const PhaseC
                     }
                     ph.y[row] = out;
                     if (row >= k0) {
+                        // K rows [kv head][stride][hd], segments swizzled by position
+                        // (k_swizzled); V transposed, [kv head][hd][stride]
                         const bool isk = row < v0;
                         const int q = row - (isk ? k0 : v0);
-                        const size_t at = (static_cast<size_t>(q / hd) * a.ctx_max + cx.P) * hd + q % hd;
+                        const size_t at = isk ? (static_cast<size_t>(q / hd) * a.kv_stride + cx.P) * hd +
+                                                    k_swizzled(q % hd, cx.P, a.kv_f16 ? 2 : 4)
+                                              : static_cast<size_t>(q) * a.kv_stride + cx.P;
                         void *cache = isk ? ph.kcache : ph.vcache;
                         if (a.kv_f16)
                             static_cast<__half *>(cache)[at] = __float2half_rn(out);
@@ -603,189 +607,39 @@ __device__ void gemv_phase(const MkParams &p, const TokenPhase &ph, const PhaseC
 
 // ------------------------------------------------------------------ attention
 
-// attention_group (tp_llama.cpp:644-690) for KV head `kvh` and its query
-// heads; the order of every sum is attn.cu's.
+constexpr int kAttnColBytes = 256;  // V^T bytes per column per chunk (attn_core.cuh)
+__host__ __device__ constexpr int mk_attn_kc(int d, int esz) { return 16384 / (d * esz); }  // K rows per chunk: 16 KB
+
+// attention_group (tp_llama.cpp:644-690) for KV head `kvh` = this CTA's
+// index, over positions 0..P: attn_core, which states the order of every
+// operation (the same code as the per-op kernel, attn.cu).
 template <int NWG, int D, int ESZ>
-__device__ void attn_phase(const MkParams &p, const TokenPhase &ph, const PhaseCtx &cx, uint8_t *smem) {
-    constexpr int kThreads = NWG * 128;
-    constexpr int kRowBytes = D * ESZ;
-    constexpr int kSegs = kRowBytes / 16;
-    constexpr int kPer = 16 / ESZ;
-    constexpr int kTC = kAttnChunk / kRowBytes;
-    constexpr int kLoads = (kAttnChunk / 16 + kThreads - 1) / kThreads;
+__device__ void attn_phase(const MkParams &p, const TokenPhase &ph, const PhaseCtx &cx, uint8_t *smem, uint64_t *bars,
+                           uint32_t &par) {
     const TokenArgs &a = p.a;
-    const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32, kvh = blockIdx.x, G = a.group;
-    uint8_t *vbuf = smem + p.off_attn;                                       // 2 x 16 KB
-    float *qs = reinterpret_cast<float *>(smem + p.off_attn + 2 * kAttnChunk);  // [4][D]
-    float *misc = qs + 4 * D;                                                // 160 floats
-    float *sc = reinterpret_cast<float *>(smem + p.off_sc);                  // [G][ctx_max]
-    const int n = cx.P + 1, nc = (n + kTC - 1) / kTC;
-    const uint8_t *kb = static_cast<const uint8_t *>(ph.kcache) + static_cast<size_t>(kvh) * a.ctx_max * kRowBytes;
-    const uint8_t *vb = static_cast<const uint8_t *>(ph.vcache) + static_cast<size_t>(kvh) * a.ctx_max * kRowBytes;
-    // this thread's first K row, q and V chunk 0 all in flight at once (rows
-    // of up to 128 bytes stay in registers; longer ones load in the loop)
-    constexpr bool kEarly = kSegs <= 8;
-    uint4 krow[kSegs];
-    if (kEarly && tid < n) {
-        const uint4 *row = reinterpret_cast<const uint4 *>(kb + static_cast<size_t>(tid) * kRowBytes);
-#pragma unroll
-        for (int sg = 0; sg < kSegs; ++sg) krow[sg] = __ldcg(row + sg);
-    }
-    for (int i = tid; i < G * D; i += kThreads) qs[i] = __ldcg(ph.q + static_cast<size_t>(kvh) * G * D + i);
-    {
-        const int bytes = min(kTC, n) * kRowBytes;
-        for (int i = tid; i < bytes / 16; i += kThreads)
-            reinterpret_cast<uint4 *>(vbuf)[i] = __ldcg(reinterpret_cast<const uint4 *>(vb) + i);
-    }
-    named_sync(1, kThreads);
-    for (int t = tid; t < n; t += kThreads) {
-        if (!kEarly || t != tid) {
-            const uint4 *row = reinterpret_cast<const uint4 *>(kb + static_cast<size_t>(t) * kRowBytes);
-#pragma unroll
-            for (int sg = 0; sg < kSegs; ++sg) krow[sg] = __ldcg(row + sg);
-        }
-        float acc4[4][4];
-#pragma unroll
-        for (int b = 0; b < 4; ++b) acc4[b][0] = acc4[b][1] = acc4[b][2] = acc4[b][3] = 0.0f;
-#pragma unroll
-        for (int sg = 0; sg < kSegs; ++sg) {
-            const uint4 raw = krow[sg];
-            float f[8];
-            if constexpr (ESZ == 2) {
-                const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float2 t2 = __half22float2(h[j]);
-                    f[2 * j] = t2.x;
-                    f[2 * j + 1] = t2.y;
-                }
-            } else {
-                f[0] = __uint_as_float(raw.x);
-                f[1] = __uint_as_float(raw.y);
-                f[2] = __uint_as_float(raw.z);
-                f[3] = __uint_as_float(raw.w);
-            }
-#pragma unroll
-            for (int b = 0; b < 4; ++b)
-                if (b < G) {
-                    const float *qb = qs + b * D + sg * kPer;
-#pragma unroll
-                    for (int e = 0; e < kPer; ++e) acc4[b][e & 3] = __fmaf_rn(f[e], qb[e], acc4[b][e & 3]);
-                }
-        }
-#pragma unroll
-        for (int b = 0; b < 4; ++b)
-            if (b < G)
-                sc[b * a.ctx_max + t] =
-                    __fmul_rn(__fadd_rn(__fadd_rn(acc4[b][0], acc4[b][1]), __fadd_rn(acc4[b][2], acc4[b][3])), a.scale);
-    }
-    named_sync(1, kThreads);
-    for (int b = 0; b < G; ++b) {
-        float m = -1e30f;
-        for (int t = tid; t < n; t += kThreads) {
-            const float v = sc[b * a.ctx_max + t];
-            m = v > m ? v : m;
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-            const float o = __shfl_xor_sync(kFullMask, m, off);
-            m = o > m ? o : m;
-        }
-        if (lane == 0) misc[b * 32 + warp] = m;
-    }
-    named_sync(1, kThreads);
-    if (tid < G) {
-        float m = -1e30f;
-        for (int w = 0; w < kThreads / 32; ++w) {
-            const float o = misc[tid * 32 + w];
-            m = o > m ? o : m;
-        }
-        misc[144 + tid] = m;
-    }
-    named_sync(1, kThreads);
-    for (int b = 0; b < G; ++b) {
-        const float mx = misc[144 + b];
-        for (int t = tid; t < n; t += kThreads) sc[b * a.ctx_max + t] = v_expf(__fsub_rn(sc[b * a.ctx_max + t], mx));
-    }
-    named_sync(1, kThreads);
-    const int n4 = n & ~3;
-    if (tid < 4 * G) {
-        const int b = tid / 4, j = tid % 4;
-        const float *sp = sc + b * a.ctx_max;
-        float acc = 0.0f;
-#pragma unroll 8
-        for (int t = j; t < n4; t += 4) acc = __fadd_rn(acc, sp[t]);
-        misc[128 + tid] = acc;
-    }
-    named_sync(1, kThreads);
-    if (tid < G) {
-        const float *l = misc + 128 + 4 * tid;
-        float sum = __fadd_rn(__fadd_rn(l[0], l[1]), __fadd_rn(l[2], l[3]));
-        for (int t = n4; t < n; ++t) sum = __fadd_rn(sum, sc[tid * a.ctx_max + t]);
-        misc[148 + tid] = __fdiv_rn(1.0f, sum);
-    }
-    named_sync(1, kThreads);
-    for (int b = 0; b < G; ++b) {
-        const float inv = misc[148 + b];
-        for (int t = tid; t < n; t += kThreads) sc[b * a.ctx_max + t] = __fmul_rn(sc[b * a.ctx_max + t], inv);
-    }
-    named_sync(1, kThreads);
-    const bool chain = tid < G * D;
-    const int b = tid / D, col = tid % D;
-    float acc = 0.0f;
-    for (int c = 0; c < nc; ++c) {
-        // next chunk into registers while this one is used
-        uint4 pre[kLoads];
-        int nbytes_next = 0;
-        if (c + 1 < nc) {
-            nbytes_next = min(kTC, n - (c + 1) * kTC) * kRowBytes;
-            const uint4 *src = reinterpret_cast<const uint4 *>(vb + static_cast<size_t>(c + 1) * kAttnChunk);
-#pragma unroll
-            for (int q = 0; q < kLoads; ++q) {
-                const int i = tid + q * kThreads;
-                if (i < nbytes_next / 16) pre[q] = __ldcg(src + i);
-            }
-        }
-        if (chain) {
-            const uint8_t *ch = vbuf + (c & 1) * kAttnChunk;
-            const float *pc = sc + b * a.ctx_max + c * kTC;
-            const int rows = min(kTC, n - c * kTC);
-#pragma unroll 8
-            for (int t = 0; t < rows; ++t) {
-                float v;
-                if constexpr (ESZ == 2)
-                    v = __half2float(reinterpret_cast<const __half *>(ch + t * kRowBytes)[col]);
-                else
-                    v = reinterpret_cast<const float *>(ch + t * kRowBytes)[col];
-                acc = __fmaf_rn(v, pc[t], acc);
-            }
-        }
-        named_sync(1, kThreads);
-        if (c + 1 < nc) {
-            uint4 *dst = reinterpret_cast<uint4 *>(vbuf + ((c + 1) & 1) * kAttnChunk);
-#pragma unroll
-            for (int q = 0; q < kLoads; ++q) {
-                const int i = tid + q * kThreads;
-                if (i < nbytes_next / 16) dst[i] = pre[q];
-            }
-        }
-        named_sync(1, kThreads);
-    }
-    if (chain) ph.out[(static_cast<size_t>(kvh) * G + b) * D + col] = acc;
+    const int kvh = blockIdx.x, G = a.group;
+    const size_t head_bytes = static_cast<size_t>(a.kv_stride) * D * ESZ;
+    if (!attn_core<D, ESZ, kAttnColBytes, mk_attn_kc(D, ESZ), NWG * 128>(
+            ph.q + static_cast<size_t>(kvh) * G * D, static_cast<const uint8_t *>(ph.kcache) + kvh * head_bytes,
+            static_cast<const uint8_t *>(ph.vcache) + kvh * head_bytes, a.kv_stride, cx.P + 1, G, a.scale,
+            ph.out + static_cast<size_t>(kvh) * G * D, smem + p.off_attn, 1, bars, par, a.status, nullptr) &&
+        threadIdx.x == 0)
+        set_abort(p, kStatusStageTimeout);
 }
 
 template <int NWG>
-__device__ void attn_dispatch(const MkParams &p, const TokenPhase &ph, const PhaseCtx &cx, uint8_t *smem) {
+__device__ void attn_dispatch(const MkParams &p, const TokenPhase &ph, const PhaseCtx &cx, uint8_t *smem, uint64_t *bars,
+                              uint32_t &par) {
     if (p.a.head_dim == 64) {
         if (p.a.kv_f16)
-            attn_phase<NWG, 64, 2>(p, ph, cx, smem);
+            attn_phase<NWG, 64, 2>(p, ph, cx, smem, bars, par);
         else
-            attn_phase<NWG, 64, 4>(p, ph, cx, smem);
+            attn_phase<NWG, 64, 4>(p, ph, cx, smem, bars, par);
     } else {
         if (p.a.kv_f16)
-            attn_phase<NWG, 128, 2>(p, ph, cx, smem);
+            attn_phase<NWG, 128, 2>(p, ph, cx, smem, bars, par);
         else
-            attn_phase<NWG, 128, 4>(p, ph, cx, smem);
+            attn_phase<NWG, 128, 4>(p, ph, cx, smem, bars, par);
     }
 }
 
@@ -796,6 +650,7 @@ __global__ void __launch_bounds__(NWG * 128 + 32, 1) token_kernel(const __grid_c
     constexpr int kThreads = NWG * 128;
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t full[kMaxRing], empty[kMaxRing];
+    __shared__ uint64_t abar[kAttnBars];  // attention's V^T and K stages
     __shared__ float s_f;
     __shared__ int s_exact, s_stop, s_tok;
     __shared__ int s_fail[4];
@@ -808,6 +663,7 @@ __global__ void __launch_bounds__(NWG * 128 + 32, 1) token_kernel(const __grid_c
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
+        for (int i = 0; i < kAttnBars; ++i) mbar_init(&abar[i], 1);
         fence_mbar_init();
         s_stop = 0;
         s_fail[0] = s_fail[1] = s_fail[2] = s_fail[3] = 0;
@@ -821,6 +677,7 @@ __global__ void __launch_bounds__(NWG * 128 + 32, 1) token_kernel(const __grid_c
     const uint32_t step0 = *reinterpret_cast<volatile unsigned *>(a.step);
     const int n_prompt = *a.n_prompt;
     uint32_t s = 0;
+    uint32_t apar = 0;  // attention stage parities (attn_core)
     int cur_tok = 0;
     for (int t = 0; t < a.ntokens; ++t) {
         PhaseCtx cx;
@@ -842,7 +699,7 @@ __global__ void __launch_bounds__(NWG * 128 + 32, 1) token_kernel(const __grid_c
             if (ph.kind == kPhGemv)
                 gemv_phase<NWG>(p, ph, cx, smem, ring, full, empty, s, &s_f, &s_exact, s_fail, t, i);
             else if (static_cast<int>(blockIdx.x) < a.kvh_local)
-                attn_dispatch<NWG>(p, ph, cx, smem);
+                attn_dispatch<NWG>(p, ph, cx, smem, abar, apar);
             named_sync(1, kThreads);
             stamp(a, t, i, 3);
             if (tid == 0) {
@@ -970,8 +827,10 @@ int make_params(const TokenArgs &a, MkParams *out, int *smem_bytes, int *wgs_out
     q.off_dred = carve(32 * 8);
     q.off_red = carve(wgs * 2 * kMaxBatch * 128 * 4);
     q.off_best = carve(wgs * kMaxBatch * kTileRows * 8);
-    q.off_attn = carve(2 * kAttnChunk + 4 * (4 * a.head_dim + 160));
-    q.off_sc = carve(4 * a.group * a.ctx_max);
+    if (a.kv_stride < a.ctx_max || a.kv_stride % 8) return kErrInval;
+    const int esz = a.kv_f16 ? 2 : 4;
+    q.off_attn = carve(attn_core_smem_bytes(a.head_dim, esz, kAttnColBytes, mk_attn_kc(a.head_dim, esz), wgs * 128,
+                                            a.kv_stride));
     const int fixed = off;
     const int limit = max_smem_optin() - 128 - 1024;  // alignment slack and static shared memory
     int ring = (limit - fixed) / kStage;
@@ -985,7 +844,6 @@ int make_params(const TokenArgs &a, MkParams *out, int *smem_bytes, int *wgs_out
     q.off_red += ring_bytes;
     q.off_best += ring_bytes;
     q.off_attn += ring_bytes;
-    q.off_sc += ring_bytes;
     *out = q;
     *smem_bytes = 128 + ring_bytes + fixed;
     *wgs_out = wgs;

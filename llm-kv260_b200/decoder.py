@@ -82,12 +82,19 @@ class Decoder:
         return self._read(2, self.ctx_max + 1, np.int32)
 
     def trace(self, tokens: int) -> None:
-        """Persistent mode: stamp the phases of the first `tokens` tokens of each later launch."""
+        """Persistent mode: stamp the phases of the first `tokens` tokens of each
+        later launch. Graph mode (tokens 0 or 1): stamp every launch of the last
+        token run."""
         check(lib().b200_decoder_trace(self.h, tokens), "b200_decoder_trace")
         self._trace_tokens = tokens
 
-    def read_trace(self, nphases: int, sms: int) -> np.ndarray:
-        """[tokens, phases, SMs, 8] trace values (ns) of the last traced launch (b200_decoder_trace)."""
+    def read_trace(self, nphases: int = 0, sms: int = 0) -> np.ndarray:
+        """Persistent mode: [tokens, phases, SMs, 8] trace values (ns) of the last
+        traced launch. Graph mode: [launches, 1024, 8] stamps of the last token
+        (b200_decoder_trace)."""
+        if not self.cfg.persistent:
+            nl = 5 * self.cfg.n_layer + 1
+            return self._read(7, nl * 1024 * 8, np.uint64).reshape(nl, 1024, 8)
         t = self._trace_tokens
         return self._read(7, t * nphases * sms * 8, np.uint64).reshape(t, nphases, sms, 8)
 
