@@ -117,10 +117,11 @@ B200_API int b200_decoder_read(b200_decoder_t *d, int what, void *host, uint64_t
  * Graph mode (tokens 0 or 1): every token run records its 5 * n_layer + 1
  * kernel launches (per layer q|k|v, attention, o, gate|up, down; then
  * lm_head), overwriting the previous token's -- per (launch, CTA < 1024)
- * eight stamps: 0 CTA set up, 1 the previous kernel's results visible, 2
- * input staged (attention: softmax done), 3 CTA end, and for attention 4 q
- * staged, 5 scores, 6 maxima, 7 exponentials done; read back as buffer 7
- * (uint64[launches][1024][8], zero where a launch has no such CTA or stamp).
+ * sixteen stamps: 0 CTA set up, 1 the previous kernel's results visible, 2
+ * input staged (attention: p computed), 3 CTA end, and for attention 4 q
+ * staged, 5 scores and maxima, 6 exponentials, 7 sums, 8 + 2c / 9 + 2c V
+ * chunk c (< 4) landed / consumed; read back as buffer 7
+ * (uint64[launches][1024][16], zero where a launch has no such CTA or stamp).
  * 0 turns tracing off. A B200 extension with no reference counterpart. */
 B200_API int b200_decoder_trace(b200_decoder_t *d, int tokens);
 

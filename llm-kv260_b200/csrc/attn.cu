@@ -4,7 +4,7 @@
 // which states the order of every operation).
 //
 // Before the kernel waits for its predecessor (the q|k|v GEMV that writes
-// this position's K row and V column), warp 0 asks L2 for the head's K rows
+// this position's K row and V column), the last warp asks L2 for the head's K rows
 // and V^T columns of the positions before it -- written by earlier tokens --
 // so the loads after the wait hit L2. The prefetch is a hint sized from a
 // read of the position that may be one token stale; what is read after the
@@ -57,7 +57,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
     uint64_t *rec = attn_rec(p.trace);
     pdl_launch_dependents();
     attn_stamp_at(rec, 0);
-    if (threadIdx.x < 32) {
+    if (threadIdx.x >= kAttnThreads - 32) {  // the last warp: thread 0's warp goes straight to the wait
         const int hint = *reinterpret_cast<const volatile int *>(p.pos) + 2;  // may be a token behind: a hint
         attn_prefetch_l2<D, ESZ>(kb, vtb, p.stride, hint < 1 ? 1 : (hint > p.ctx_max ? p.ctx_max : hint));
     }

@@ -102,7 +102,7 @@ __device__ __forceinline__ void attn_stamp_at(uint64_t *rec, int j) {
     if (rec && threadIdx.x == 0) rec[j] = globaltimer_ns();
 }
 
-// Warp 0 of the caller may bring this head's K rows and V^T columns for
+// One warp of the caller may bring this head's K rows and V^T columns for
 // positions [0, n_hint) into L2 ahead of time (a hint: any n_hint is safe).
 template <int D, int ESZ>
 __device__ __forceinline__ void attn_prefetch_l2(const uint8_t *kb, const uint8_t *vtb, int stride, int n_hint) {
@@ -124,7 +124,8 @@ __device__ __forceinline__ void attn_prefetch_l2(const uint8_t *kb, const uint8_
 // kStatusStageTimeout in *status; the copies in flight are then waited for
 // (bounded) and the function returns false with `out` not written.
 // rec (optional, thread 0 writes): stamps 4 q staged, 5 scores and maxima,
-// 6 exponentials, 7 sums, 2 p.
+// 6 exponentials, 7 sums, 2 p; 8 + 2c / 9 + 2c V^T chunk c (< 4) landed /
+// consumed.
 template <int D, int ESZ, int COLB, int KC, int NT>
 __device__ bool attn_core(const float *q, const uint8_t *kb, const uint8_t *vtb, int stride, int n, int G, float scale,
                           float *out, uint8_t *smem, int bar, uint64_t *bars, uint32_t &par, unsigned *status,
@@ -149,7 +150,7 @@ __device__ bool attn_core(const float *q, const uint8_t *kb, const uint8_t *vtb,
     float2 *pp = reinterpret_cast<float2 *>(e + stride);  // [2][stride]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nch = (n + kChunkPos - 1) / kChunkPos, nkc = (n + KC - 1) / KC;
-    const uint64_t pol = l2_policy_evict_normal();
+    const uint64_t pol = l2_policy_evict_last();  // the KV cache stays in L2 while the weights stream past
     uint32_t pend = 0;  // barriers with copies issued and not yet waited for (the same in every thread)
 
     // V^T chunk c into stage c % 2: thread `col` < D copies its column's
@@ -203,8 +204,6 @@ __device__ bool attn_core(const float *q, const uint8_t *kb, const uint8_t *vtb,
         if (i < G * D) qv[u] = __ldcg(q + i);
     }
     stage_k(0);
-    stage_vt(0);
-    stage_vt(1);
 #pragma unroll
     for (int u = 0; u < (4 * D + NT - 1) / NT; ++u) {
         const int i = tid + u * NT;
@@ -213,6 +212,10 @@ __device__ bool attn_core(const float *q, const uint8_t *kb, const uint8_t *vtb,
     if (tid == 0) *fail = 0;
     named_sync(bar, NT);
     attn_stamp_at(rec, 4);
+    // V^T is needed only by the output chains: its copies start after q
+    // has arrived (a load queued behind them would wait for their bytes)
+    stage_vt(0);
+    stage_vt(1);
 
     // scores (tp_llama.cpp:652-664) and this thread's maxima
     float mx[4] = {-1e30f, -1e30f, -1e30f, -1e30f};
@@ -363,43 +366,30 @@ __device__ bool attn_core(const float *q, const uint8_t *kb, const uint8_t *vtb,
         const int slot = c % kAttnVtStages;
         wait_bar(slot);
         named_sync(bar, NT);  // chunk c landed everywhere (and, at c = 0, every p written)
+        if (c < 4) attn_stamp_at(rec, 8 + 2 * c);
         if (*reinterpret_cast<volatile int *>(fail)) return drain();
         if (chain) {
             // groups of kPer positions: one 16-byte V load and kPer / 2
-            // 16-byte p loads, the next group's loads issued before this
-            // group's fused multiply-adds (each accumulator is one chain)
+            // 16-byte p loads (2 positions of the head pair each) feed one
+            // fused multiply-add per position and head, in order
             const uint8_t *vc = vt + slot * kStageBytes + col * kColStride;
             const float4 *pc = reinterpret_cast<const float4 *>(pp + (h0 / 2) * stride + c * kChunkPos);
             const int rows = min(kChunkPos, n - c * kChunkPos), full = rows / kPer * kPer;
             int t = 0;
-            if (full > 0) {
-                uint4 vr = *reinterpret_cast<const uint4 *>(vc);
+#pragma unroll 4
+            for (; t < full; t += kPer) {
+                const uint4 vr = *reinterpret_cast<const uint4 *>(vc + t * ESZ);
                 float4 pr[kPer / 2];
 #pragma unroll
-                for (int k = 0; k < kPer / 2; ++k) pr[k] = pc[k];
-                for (;;) {
-                    const bool more = t + kPer < full;
-                    uint4 vn = vr;
-                    float4 pn[kPer / 2];
-                    if (more) {
-                        vn = *reinterpret_cast<const uint4 *>(vc + (t + kPer) * ESZ);
+                for (int k = 0; k < kPer / 2; ++k) pr[k] = pc[t / 2 + k];
+                float v[8];
+                attn_seg_floats<ESZ>(vr, v);
 #pragma unroll
-                        for (int k = 0; k < kPer / 2; ++k) pn[k] = pc[(t + kPer) / 2 + k];
-                    }
-                    float v[8];
-                    attn_seg_floats<ESZ>(vr, v);
-#pragma unroll
-                    for (int k = 0; k < kPer / 2; ++k) {
-                        acc0 = __fmaf_rn(v[2 * k], pr[k].x, acc0);
-                        acc1 = __fmaf_rn(v[2 * k], pr[k].y, acc1);
-                        acc0 = __fmaf_rn(v[2 * k + 1], pr[k].z, acc0);
-                        acc1 = __fmaf_rn(v[2 * k + 1], pr[k].w, acc1);
-                    }
-                    t += kPer;
-                    if (!more) break;
-                    vr = vn;
-#pragma unroll
-                    for (int k = 0; k < kPer / 2; ++k) pr[k] = pn[k];
+                for (int k = 0; k < kPer / 2; ++k) {
+                    acc0 = __fmaf_rn(v[2 * k], pr[k].x, acc0);
+                    acc1 = __fmaf_rn(v[2 * k], pr[k].y, acc1);
+                    acc0 = __fmaf_rn(v[2 * k + 1], pr[k].z, acc0);
+                    acc1 = __fmaf_rn(v[2 * k + 1], pr[k].w, acc1);
                 }
             }
             const float2 *pc2 = reinterpret_cast<const float2 *>(pc);
@@ -411,6 +401,7 @@ __device__ bool attn_core(const float *q, const uint8_t *kb, const uint8_t *vtb,
             }
         }
         named_sync(bar, NT);  // chunk c consumed
+        if (c < 4) attn_stamp_at(rec, 9 + 2 * c);
         stage_vt(c + kAttnVtStages);
     }
     if (chain) {

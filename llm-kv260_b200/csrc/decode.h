@@ -25,7 +25,7 @@ struct AttnLaunch {
     int kv_f16 = 1;
     float scale = 0.0f;             // 1 / sqrtf(head_dim)
     bool pdl = true;
-    uint64_t *trace = nullptr;      // optional launch trace (q4gemv.h, kTraceCtas); stamp 2 = softmax done
+    uint64_t *trace = nullptr;      // optional launch trace (q4gemv.h, kTraceCtas)
 };
 
 int attn_kv_stride(int ctx_max);  // ctx_max rounded up to a multiple of 8

@@ -763,7 +763,8 @@ extern "C" int b200_decoder_trace(b200_decoder_t *d, int tokens) {
         // graph mode: the launches of the last token run, recorded by every replay
         if (tokens > 1) return dfail(kErrInval, "decoder: graph mode traces one token (the last one run)");
         if (int rc = use_dev(d)) return rc;
-        if (cudaStreamSynchronize(d->stream) != cudaSuccess) return dfail(kErrCuda, "decoder: stream failed");
+        if (cudaStreamSynchronize(d->stream) != cudaSuccess)
+            return dfail(kErrCuda, "decoder: stream failed: %s", cudaGetErrorString(cudaGetLastError()));
         const int nl = 5 * d->c.n_layer + 1;
         if (tokens && !d->trace_launches) {
             const size_t bytes = static_cast<size_t>(nl) * kTraceCtas * kTraceStamps * 8;

@@ -103,13 +103,15 @@ enum Epilogue : int {
 constexpr int kMaxDecodeRanks = 8;
 
 // Optional launch trace of the decoder's per-op kernels: thread 0 of CTA b
-// (b < kTraceCtas) writes global-timer stamps (ns) at trace[b * 8 + j]:
+// (b < kTraceCtas) writes global-timer stamps (ns) at trace[b * 16 + j]:
 // 0 after the CTA's set-up, 1 when the previous kernel's results are visible
-// (griddepcontrol.wait returned), 2 when its input is staged (attention: the
-// softmax done), 3 at its end; attention also 4 q staged, 5 scores done,
-// 6 maxima done, 7 exponentials done.
+// (griddepcontrol.wait returned), 2 when its input is staged (attention: p
+// computed), 3 at its end; the tile GEMV also 4 its first weight stage
+// landed, 5 its row groups done (thread 0's quad); attention 4 q staged,
+// 5 scores and maxima, 6 exponentials, 7 sums, 8 + 2c / 9 + 2c V^T chunk c
+// (< 4) landed / consumed.
 constexpr int kTraceCtas = 1024;
-constexpr int kTraceStamps = 8;
+constexpr int kTraceStamps = 16;
 
 struct DecodeOps {
     int pro = kProPlain;
@@ -154,7 +156,7 @@ struct TileLaunch {
     int sel_base = 0;
     void *sel_scratch = nullptr;  // tile_select_scratch_bytes(), ticket zeroed once
     DecodeOps dec;                // decoder prologue/epilogue (plain GEMV by default)
-    uint64_t *trace = nullptr;    // optional: [CTA < kTraceCtas][4] global-timer stamps (kTraceStamps)
+    uint64_t *trace = nullptr;    // optional: [CTA < kTraceCtas][kTraceStamps] global-timer stamps
 };
 int tile_select_scratch_bytes();
 

@@ -86,6 +86,22 @@ __device__ __forceinline__ uint64_t ld_word(const uint64_t *p) {
 // consumers allow for k/32 blocks.
 __device__ __forceinline__ int stage_tpb(int nb) { return nb * 4 <= kConsumers ? 4 : (nb * 2 <= kConsumers ? 2 : 1); }
 
+// RMSNorm's sequential fallback (tp_llama.cpp:560-564): lane j sums x[i]^2
+// for i = j, j+4, ... in order, threads 0-3, then (l0 + l2) + (l1 + l3);
+// returns (float)(ss / k). Out of line: rarely taken, and the hot code stays
+// small (each launch fetches its instructions anew).
+__device__ __noinline__ float rms_sequential(const float *xf, double *dred, int k) {
+    const int t = threadIdx.x;
+    if (t < 4) {
+        double a = 0.0;
+        for (int i = t; i < k; i += 4) a = __dadd_rn(a, __dmul_rn(static_cast<double>(xf[i]), static_cast<double>(xf[i])));
+        dred[8 + t] = a;
+    }
+    named_sync(1, kConsumers);
+    const double ss2 = __dadd_rn(__dadd_rn(dred[8], dred[10]), __dadd_rn(dred[9], dred[11]));
+    return __double2float_rn(__ddiv_rn(ss2, static_cast<double>(k)));
+}
+
 // Consumer side of staging a float32 x into xs (int8[k], then (float32 d,
 // int32 sum) per block -- stage_x's layout), TPB threads per 32-block with
 // E = 32 / TPB consecutive values each. The prologue's x is the plain input,
@@ -99,13 +115,13 @@ __device__ __forceinline__ int stage_tpb(int nb) { return nb * 4 <= kConsumers ?
 // block's Q8_0 quantisation (q4_0.py:83-97) meets its maximum and its int
 // sum across the block's TPB adjacent lanes by xor shuffles: the maximum
 // (fmaxf) and an integer sum do not depend on the order.
-template <int TPB>
+template <int TPB, int PRO>
 __device__ __forceinline__ void stage_x_f32(const TileParams &p, uint8_t *xs, float *xf, double *dred) {
     constexpr int E = 32 / TPB;
     const int k = p.k, nb = k / kQK, t = threadIdx.x, b = t / TPB, r = t % TPB, lane = t % 32, warp = t / 32;
     const bool live = b < nb;
     const int i0 = 32 * b + E * r;
-    const int pro = p.dec.pro;
+    constexpr int pro = PRO;
     float w[E];
     if (pro != kProPlain && live) {
         const float4 *wv = reinterpret_cast<const float4 *>(p.dec.norm_w + i0);
@@ -170,17 +186,7 @@ __device__ __forceinline__ void stage_x_f32(const TileParams &p, uint8_t *xs, fl
         for (int w8 = 0; w8 < kConsumers / 32; ++w8) tot = __dadd_rn(tot, dred[w8]);
         const double q = __ddiv_rn(tot, static_cast<double>(k));
         float f = __double2float_rn(q);
-        if (p.dec.exact_norm || !rms_float_is_safe(q, f, k)) {
-            // tp_llama.cpp:560-564: lane j sums x[i]^2 for i = j, j+4, ... in order
-            if (t < 4) {
-                double a = 0.0;
-                for (int i = t; i < k; i += 4) a = __dadd_rn(a, __dmul_rn(static_cast<double>(xf[i]), static_cast<double>(xf[i])));
-                dred[8 + t] = a;
-            }
-            named_sync(1, kConsumers);
-            const double ss2 = __dadd_rn(__dadd_rn(dred[8], dred[10]), __dadd_rn(dred[9], dred[11]));
-            f = __double2float_rn(__ddiv_rn(ss2, static_cast<double>(k)));
-        }
+        if (p.dec.exact_norm || !rms_float_is_safe(q, f, k)) f = rms_sequential(xf, dred, k);
         const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(f, p.dec.eps)));
 #pragma unroll
         for (int j = 0; j < E; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], scale), w[j]);
@@ -259,7 +265,11 @@ __device__ __forceinline__ bool ring_wait(uint64_t *bar, uint32_t parity, unsign
 }
 
 // XREG: K <= 2048, each thread's 8 x blocks stay in registers.
-template <int XMODE, bool XREG>
+// One instantiation per (x mode, x in registers, prologue, epilogue, fused
+// pick) that a caller uses (pick_tile): each launch runs a compact,
+// contiguous code path -- a kernel holding every variant is several times
+// larger than an SM's instruction cache keeps across the token's launches.
+template <int XMODE, bool XREG, int PRO, int EPI, bool PICK>
 __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_constant__ TileParams p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t full[kMaxStages], empty[kMaxStages];
@@ -315,13 +325,16 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
     if constexpr (XMODE == kXF32) {
         float *xf = reinterpret_cast<float *>(xs + xarea_bytes(p.k));    // with a norm prologue only
         double *dred = reinterpret_cast<double *>(xs + xarea_bytes(p.k) + 4 * p.k);
-        const int tpb = stage_tpb(p.nb);
-        if (tpb == 4)
-            stage_x_f32<4>(p, xs, xf, dred);
-        else if (tpb == 2)
-            stage_x_f32<2>(p, xs, xf, dred);
-        else
-            stage_x_f32<1>(p, xs, xf, dred);
+        // K <= 2048 (XREG) always stages with 4 threads per block; only the
+        // variants a kernel can reach are compiled into it
+        if constexpr (XREG) {
+            stage_x_f32<4, PRO>(p, xs, xf, dred);
+        } else {
+            if (stage_tpb(p.nb) == 2)
+                stage_x_f32<2, PRO>(p, xs, xf, dred);
+            else
+                stage_x_f32<1, PRO>(p, xs, xf, dred);
+        }
     } else {
         pdl_wait_prior_grid();
         trace_stamp(p.trace, 1);
@@ -329,7 +342,6 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
     }
     named_sync(1, kConsumers);
     trace_stamp(p.trace, 2);
-
     const int quad = warp / 4, i = (warp % 4) * 4 + (lane >> 3), l = lane & 7;
     XBlock xr[XREG ? kXregChunks : 1];
     if constexpr (XREG) {
@@ -337,7 +349,7 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
         for (int c = 0; c < kXregChunks; ++c)
             if (c < p.nch) load_xblock_smem(xs, p.k, 8 * c + l, xr[c]);
     }
-    const int epi = p.dec.epi;
+    constexpr int epi = EPI;
     const int dpos = (epi == kEpiRopeKv) ? *p.dec.pos : 0;
     const bool xchg = epi == kEpiResidual && p.dec.nranks > 1;
     uint32_t epoch = 0;
@@ -356,6 +368,7 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
             ok = false;
             break;
         }
+        if (s == quad) trace_stamp(p.trace, 4);
         const uint8_t *tiles = ring + static_cast<size_t>(slot) * p.slot_bytes;
         float acc = 0.0f;
         if constexpr (XREG) {
@@ -381,7 +394,7 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
         if (epi == kEpiStore) {
             if (live) {
                 p.y[row] = yv;
-                if (sel_better(yv, row, best_v, best_i)) {
+                if (PICK && sel_better(yv, row, best_v, best_i)) {
                     best_v = yv;
                     best_i = row;
                 }
@@ -432,6 +445,7 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
             }
         }
     }
+    trace_stamp(p.trace, 5);
     if (xchg && ok && l == 0) {
         // Every rank computed these rows' partials for its K slice; collect
         // them from this rank's window and sum in rank order
@@ -463,7 +477,7 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
             p.dec.res[row] = __fadd_rn(p.dec.res[row], sum);
         }
     }
-    if (p.sel_out) {
+    if constexpr (PICK) {
         // CTA best over the row threads (l == 0), then the last CTA to finish
         // reduces all CTAs' bests
         if (l == 0) s_best[t / kLanes] = make_float2(best_v, __int_as_float(best_i));
@@ -565,9 +579,27 @@ __global__ void repack_tiles_kernel(const uint8_t *__restrict__ src, int rows, i
 
 using TileKernelFn = void (*)(TileParams);
 
-TileKernelFn pick_tile(int xmode, bool xreg) {
-    if (xmode == kXF32) return xreg ? q4_tile_kernel<kXF32, true> : q4_tile_kernel<kXF32, false>;
-    return xreg ? q4_tile_kernel<kXPacked, true> : q4_tile_kernel<kXPacked, false>;
+template <int XMODE, int PRO, int EPI, bool PICK>
+TileKernelFn tile_fn(bool xreg) {
+    return xreg ? q4_tile_kernel<XMODE, true, PRO, EPI, PICK> : q4_tile_kernel<XMODE, false, PRO, EPI, PICK>;
+}
+
+// The instantiations callers use: the engine's plain GEMV (with or without
+// the fused pick) for both x modes, and the decoder's five launch kinds.
+// Any other combination is refused.
+TileKernelFn pick_tile(int xmode, bool xreg, int pro, int epi, bool pick) {
+    if (pro == kProPlain && epi == kEpiStore) {
+        if (xmode == kXPacked) return pick ? tile_fn<kXPacked, kProPlain, kEpiStore, true>(xreg)
+                                           : tile_fn<kXPacked, kProPlain, kEpiStore, false>(xreg);
+        return pick ? tile_fn<kXF32, kProPlain, kEpiStore, true>(xreg) : tile_fn<kXF32, kProPlain, kEpiStore, false>(xreg);
+    }
+    if (xmode != kXF32) return nullptr;
+    if (pro == kProEmbedNorm && epi == kEpiRopeKv && !pick) return tile_fn<kXF32, kProEmbedNorm, kEpiRopeKv, false>(xreg);
+    if (pro == kProRmsnorm && epi == kEpiRopeKv && !pick) return tile_fn<kXF32, kProRmsnorm, kEpiRopeKv, false>(xreg);
+    if (pro == kProPlain && epi == kEpiResidual && !pick) return tile_fn<kXF32, kProPlain, kEpiResidual, false>(xreg);
+    if (pro == kProRmsnorm && epi == kEpiSiluPairs && !pick) return tile_fn<kXF32, kProRmsnorm, kEpiSiluPairs, false>(xreg);
+    if (pro == kProRmsnorm && epi == kEpiStore && pick) return tile_fn<kXF32, kProRmsnorm, kEpiStore, true>(xreg);
+    return nullptr;
 }
 
 struct TilePlan {
@@ -583,7 +615,8 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
     if (int rc = tile_validate(L, &why)) return rc;
     const int nb = L.k / kQK, nch = nb / kLanes;
     if (nb > kConsumers) return kErrInval;  // x staging: one consumer thread per block
-    TileKernelFn fn = pick_tile(L.xmode, nch <= kXregChunks);
+    TileKernelFn fn = pick_tile(L.xmode, nch <= kXregChunks, L.dec.pro, L.dec.epi, L.sel_out != nullptr);
+    if (!fn) return kErrInval;  // a prologue / epilogue / pick combination no caller uses
     TileParams p{};
     p.w = L.w;
     p.y = L.y;

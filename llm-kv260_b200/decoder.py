@@ -90,11 +90,11 @@ class Decoder:
 
     def read_trace(self, nphases: int = 0, sms: int = 0) -> np.ndarray:
         """Persistent mode: [tokens, phases, SMs, 8] trace values (ns) of the last
-        traced launch. Graph mode: [launches, 1024, 8] stamps of the last token
+        traced launch. Graph mode: [launches, 1024, 16] stamps of the last token
         (b200_decoder_trace)."""
         if not self.cfg.persistent:
             nl = 5 * self.cfg.n_layer + 1
-            return self._read(7, nl * 1024 * 8, np.uint64).reshape(nl, 1024, 8)
+            return self._read(7, nl * 1024 * 16, np.uint64).reshape(nl, 1024, 16)
         t = self._trace_tokens
         return self._read(7, t * nphases * sms * 8, np.uint64).reshape(t, nphases, sms, 8)
 
