@@ -1,14 +1,32 @@
 // Decode attention for one layer, bit-exact to the reference runtime's
 // attention_group (board/tp/tp_llama.cpp:644-690) over this rank's heads:
-// one CTA of kAttnThreads per local KV head running attn_core (attn_core.cuh,
-// which states the order of every operation).
+// the per-op decoder's kernel. (The persistent kernel runs the single-CTA
+// attn_core of attn_core.cuh; the arithmetic and its order are the same.)
 //
-// Before the kernel waits for its predecessor (the q|k|v GEMV that writes
-// this position's K row and V column), the last warp asks L2 for the head's K rows
-// and V^T columns of the positions before it -- written by earlier tokens --
-// so the loads after the wait hit L2. The prefetch is a hint sized from a
-// read of the position that may be one token stale; what is read after the
-// wait is the current data either way (L2 is the point of coherence).
+// One thread-block cluster of kSplit CTAs per local KV head. CTA r of the
+// cluster:
+//   scores  the positions [r * per, (r + 1) * per) (per = ceil(n / kSplit)):
+//           its K rows land in shared memory by one bulk copy (rows swizzled
+//           by position, k_swizzled), one thread per position as attn_core
+//           does, and every score row (4 heads) goes to every CTA of the
+//           cluster through distributed shared memory; one cluster barrier;
+//   softmax every CTA then holds all n scores and runs the reference's max,
+//           v_expf, four-lane sums and 1 / sum itself -- the same operations
+//           in the same order on the same values, so the same bits;
+//   output  the columns [r * D / kSplit, (r + 1) * D / kSplit): their V^T
+//           bytes land by one bulk copy per column, and one thread per
+//           (column, head) runs the output's fused multiply-add chain over
+//           t = 0..n-1 in order.
+// Each CTA moves a kSplit-th of the head's K and V bytes and computes a
+// kSplit-th of its scores: the single-CTA kernel was bound by one SM's
+// ingest and shared-memory broadcasts. No TMA multicast: every copy is a
+// plain 1-D bulk copy of this GPU's memory into this CTA's shared memory.
+//
+// Before the dependency wait, the last warp asks L2 for this CTA's K rows
+// and V^T columns of the positions before the current one (a hint sized
+// from a position read that may be one token stale; what is read after the
+// wait is current either way). Every CTA reaches both cluster barriers on
+// every path, failure included, and every mbarrier wait is bounded.
 #include <cuda_fp16.h>
 
 #include "attn_core.cuh"
@@ -20,14 +38,11 @@ namespace b200 {
 namespace {
 
 constexpr int kAttnThreads = 256;
-
-// V^T bytes per column per chunk, and K rows per chunk (64 KB of K)
-__host__ __device__ constexpr int attn_colb(int d) { return d == 64 ? 512 : 256; }
-__host__ __device__ constexpr int attn_kc(int d, int esz) { return 65536 / (d * esz); }
+constexpr int kSplit = 4;  // CTAs per KV head: the cluster size
 
 struct AttnParams {
     const float *q;
-    const uint8_t *kcache, *vcache;  // this layer: K [kv head][stride][D], V^T [kv head][D][stride]
+    const uint8_t *kcache, *vcache;  // this layer: K [kv head][stride][D] (swizzled), V^T [kv head][D][stride]
     float *out;
     const int *pos;
     unsigned *status;
@@ -36,40 +51,275 @@ struct AttnParams {
     uint64_t *trace;  // optional launch trace (q4gemv.h, kTraceCtas)
 };
 
+// Shared-memory layout of one CTA (byte offsets, 16-byte aligned pieces).
+struct AttnSmem {
+    int kbuf, vt, qs, part, hinv, e, pv, total;
+    int slice_rows;  // K rows a CTA stages at most
+    int col_stride;  // bytes between two V^T columns: an odd number of 16-byte units
+};
+
+__host__ __device__ inline AttnSmem attn_smem_layout(int d, int esz, int stride) {
+    AttnSmem L{};
+    const int cw = d / kSplit;
+    L.slice_rows = (stride + kSplit - 1) / kSplit;
+    L.col_stride = ((stride * esz / 16) | 1) * 16;
+    int off = 0;
+    auto carve = [&](int bytes) {
+        const int at = off;
+        off += (bytes + 15) / 16 * 16;
+        return at;
+    };
+    L.kbuf = carve(L.slice_rows * d * esz);
+    L.vt = carve(cw * L.col_stride);
+    L.qs = carve(4 * d * 4);
+    L.part = carve((kAttnThreads / 32) * 16);
+    L.hinv = carve(32);
+    L.e = carve(16 * stride);
+    L.pv = carve(16 * stride);
+    L.total = off;
+    return L;
+}
+
 __device__ __forceinline__ uint64_t *attn_rec(uint64_t *trace) {
     return (trace && blockIdx.x < kTraceCtas) ? trace + blockIdx.x * kTraceStamps : nullptr;
 }
 
 template <int D, int ESZ>
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_constant__ AttnParams p) {
-    extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t bars[kAttnBars];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-    const int kvh = blockIdx.x, G = p.group;
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kAttnBars; ++s) mbar_init(&bars[s], 1);
-        fence_mbar_init();
-    }
-    __syncthreads();
+    constexpr int kRowBytes = D * ESZ;
+    constexpr int kSegs = kRowBytes / 16;
+    constexpr int kPer = 16 / ESZ;  // elements per 16 bytes
+    constexpr int CW = D / kSplit;  // output columns per CTA
+    constexpr int kQv = (4 * D + kAttnThreads - 1) / kAttnThreads;
+    static_assert(kSegs % 8 == 0 && kPer % 4 == 0 && 4 * CW <= kAttnThreads, "attention shape");
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t bars[2];  // 0: this CTA's V^T columns, 1: its K rows
+    __shared__ int s_fail;
+    const AttnSmem S = attn_smem_layout(D, ESZ, p.stride);
+    uint8_t *kbuf = smem + S.kbuf, *vt = smem + S.vt;
+    float *qs = reinterpret_cast<float *>(smem + S.qs);
+    float *part = reinterpret_cast<float *>(smem + S.part);
+    float *hinv = reinterpret_cast<float *>(smem + S.hinv);
+    float4 *e = reinterpret_cast<float4 *>(smem + S.e);  // [position]: the 4 heads' scores, then exponentials
+    float *pv = reinterpret_cast<float *>(smem + S.pv);   // [head][position]: p
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, G = p.group;
+    const int kvh = blockIdx.x / kSplit;
+    const int r = static_cast<int>(cluster_ctarank());
+    const int c0 = r * CW;
     const size_t head_bytes = static_cast<size_t>(p.stride) * D * ESZ;
     const uint8_t *kb = p.kcache + kvh * head_bytes;
-    const uint8_t *vtb = p.vcache + kvh * head_bytes;
+    const uint8_t *vtb = p.vcache + kvh * head_bytes;  // column c at c * stride * ESZ
     uint64_t *rec = attn_rec(p.trace);
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+        s_fail = 0;
+    }
+    __syncthreads();
     pdl_launch_dependents();
     attn_stamp_at(rec, 0);
-    if (threadIdx.x >= kAttnThreads - 32) {  // the last warp: thread 0's warp goes straight to the wait
-        const int hint = *reinterpret_cast<const volatile int *>(p.pos) + 2;  // may be a token behind: a hint
-        attn_prefetch_l2<D, ESZ>(kb, vtb, p.stride, hint < 1 ? 1 : (hint > p.ctx_max ? p.ctx_max : hint));
+    if (tid >= kAttnThreads - 32) {  // L2 hint: this CTA's K rows and V^T columns, earlier positions
+        int hint = *reinterpret_cast<const volatile int *>(p.pos) + 2;  // may be a token behind
+        hint = hint < 1 ? 1 : (hint > p.ctx_max ? p.ctx_max : hint);
+        const int hp = (hint + kSplit - 1) / kSplit, h0 = min(hint, r * hp), h1 = min(hint, h0 + hp);
+        if (lane == 0 && h1 > h0)
+            bulk_prefetch_l2(kb + static_cast<size_t>(h0) * kRowBytes, static_cast<uint32_t>((h1 - h0) * kRowBytes));
+        const uint32_t hb = static_cast<uint32_t>((hint * ESZ + 15) / 16 * 16);
+        for (int j = lane; j < CW; j += 32) bulk_prefetch_l2(vtb + static_cast<size_t>(c0 + j) * p.stride * ESZ, hb);
     }
+    cluster_sync_all();  // every CTA of the cluster runs before any store into its shared memory
     pdl_wait_prior_grid();
     attn_stamp_at(rec, 1);
+
     const int n = *p.pos + 1;
-    uint32_t par = 0;
-    (void)attn_core<D, ESZ, attn_colb(D), attn_kc(D, ESZ), kAttnThreads>(
-        p.q + static_cast<size_t>(kvh) * G * D, kb, vtb, p.stride, n, G, p.scale,
-        p.out + static_cast<size_t>(kvh) * G * D, smem, 1, bars, par, p.status, rec);
+    const int per = (n + kSplit - 1) / kSplit;
+    const int r0 = min(n, r * per), r1 = min(n, r0 + per);
+    const bool krows = r1 > r0;
+    const uint64_t pol = l2_policy_evict_last();  // the KV cache stays in L2 while the weights stream past
+    // q first (on the critical path), then this CTA's K rows in one copy
+    float qv[kQv];
+#pragma unroll
+    for (int u = 0; u < kQv; ++u) {
+        const int i = tid + u * kAttnThreads;
+        if (i < G * D) qv[u] = __ldcg(p.q + static_cast<size_t>(kvh) * G * D + i);
+    }
+    if (tid == 0 && krows) {
+        const uint32_t kbytes = static_cast<uint32_t>((r1 - r0) * kRowBytes);
+        mbar_arrive_expect_tx(&bars[1], kbytes);
+        bulk_g2s(kbuf, kb + static_cast<size_t>(r0) * kRowBytes, kbytes, &bars[1], pol);
+    }
+#pragma unroll
+    for (int u = 0; u < kQv; ++u) {
+        const int i = tid + u * kAttnThreads;
+        if (i < G * D) qs[i] = qv[u];
+    }
+    __syncthreads();
+    attn_stamp_at(rec, 4);
+    // this CTA's V^T columns, positions [0, n): one copy per column (rounded
+    // up to 16 bytes, which stays below stride: stride % 8 == 0)
+    const uint32_t colb = static_cast<uint32_t>((n * ESZ + 15) / 16 * 16);
+    if (tid == 0) mbar_arrive_expect_tx(&bars[0], colb * CW);
+    if (tid < CW)
+        bulk_g2s(vt + tid * S.col_stride, vtb + static_cast<size_t>(c0 + tid) * p.stride * ESZ, colb, &bars[0], pol);
+
+    // scores of positions [r0, r1) (tp_llama.cpp:652-664), to every CTA
+    if (krows && !wait_stage(&bars[1], 0u, p.status)) atomicExch(&s_fail, 1);
+    for (int t = r0 + tid; t < r1; t += kAttnThreads) {
+        const uint8_t *row = kbuf + (t - r0) * kRowBytes;
+        const int sw = t & 7;
+        float a[4][4];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) a[b][0] = a[b][1] = a[b][2] = a[b][3] = 0.0f;
+#pragma unroll
+        for (int s8 = 0; s8 < kSegs; s8 += 8) {
+            uint4 kr[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) kr[j] = *reinterpret_cast<const uint4 *>(row + (s8 + (j ^ sw)) * 16);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float f[8];
+                attn_seg_floats<ESZ>(kr[j], f);
+                const int i0 = (s8 + j) * kPer;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    if (b < G) {
+#pragma unroll
+                        for (int m4 = 0; m4 < kPer; m4 += 4) {
+                            const float4 q4 = lds_f4(qs + b * D + i0 + m4);
+                            a[b][0] = __fmaf_rn(f[m4], q4.x, a[b][0]);
+                            a[b][1] = __fmaf_rn(f[m4 + 1], q4.y, a[b][1]);
+                            a[b][2] = __fmaf_rn(f[m4 + 2], q4.z, a[b][2]);
+                            a[b][3] = __fmaf_rn(f[m4 + 3], q4.w, a[b][3]);
+                        }
+                    }
+                }
+            }
+        }
+        float sv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+            if (b < G) sv[b] = __fmul_rn(__fadd_rn(__fadd_rn(a[b][0], a[b][1]), __fadd_rn(a[b][2], a[b][3])), p.scale);
+        const float4 s4 = make_float4(sv[0], sv[1], sv[2], sv[3]);
+#pragma unroll
+        for (int q = 0; q < kSplit; ++q) st_cluster_f4(cluster_map(&e[t], static_cast<uint32_t>(q)), s4);
+    }
+    cluster_sync_all();  // every CTA now holds all n scores
+    attn_stamp_at(rec, 5);
+
+    // running max per head over all positions (exact, so any tree of `>`
+    // gives the reference's value), then the exponentials
+    float mx[4] = {-1e30f, -1e30f, -1e30f, -1e30f};
+    for (int t = tid; t < n; t += kAttnThreads) {
+        const float4 s = e[t];
+        mx[0] = attn_max_gt(mx[0], s.x);
+        mx[1] = attn_max_gt(mx[1], s.y);
+        mx[2] = attn_max_gt(mx[2], s.z);
+        mx[3] = attn_max_gt(mx[3], s.w);
+    }
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        if (b < G) {
+            float m = mx[b];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) m = attn_max_gt(m, __shfl_xor_sync(kFullMask, m, off));
+            if (lane == 0) part[warp * 4 + b] = m;
+        }
+    }
+    __syncthreads();
+    float m[4] = {-1e30f, -1e30f, -1e30f, -1e30f};
+    for (int w = 0; w < kAttnThreads / 32; ++w) {
+        const float4 pw = *reinterpret_cast<const float4 *>(part + w * 4);
+        m[0] = attn_max_gt(m[0], pw.x);
+        m[1] = attn_max_gt(m[1], pw.y);
+        m[2] = attn_max_gt(m[2], pw.z);
+        m[3] = attn_max_gt(m[3], pw.w);
+    }
+    for (int t = tid; t < n; t += kAttnThreads) {
+        float4 s = e[t];
+        s.x = v_expf(__fsub_rn(s.x, m[0]));
+        if (G > 1) s.y = v_expf(__fsub_rn(s.y, m[1]));
+        if (G > 2) s.z = v_expf(__fsub_rn(s.z, m[2]));
+        if (G > 3) s.w = v_expf(__fsub_rn(s.w, m[3]));
+        e[t] = s;
+    }
+    __syncthreads();
+    attn_stamp_at(rec, 6);
+
+    // sums (softmax_exp, tp_llama.cpp:626-633): warp 0, lane 4 * head + j
+    // adds positions j, j+4, ... below n - n % 4 in order; (l0 + l1) + (l2 + l3)
+    // by two xor shuffles; then the tail one by one; inv = 1 / sum
+    if (warp == 0) {
+        const int b = lane >> 2, j4 = lane & 3, n4 = n & ~3;
+        const float *col = reinterpret_cast<const float *>(e) + b;
+        float acc = 0.0f;
+        if (b < G) {
+#pragma unroll 8
+            for (int t = j4; t < n4; t += 4) acc = __fadd_rn(acc, col[4 * t]);
+        }
+        const float x = __fadd_rn(acc, __shfl_xor_sync(kFullMask, acc, 1));
+        const float y = __fadd_rn(x, __shfl_xor_sync(kFullMask, x, 2));
+        if (b < G && j4 == 0) {
+            float sum = y;
+            for (int t = n4; t < n; ++t) sum = __fadd_rn(sum, col[4 * t]);
+            hinv[b] = __fdiv_rn(1.0f, sum);
+        }
+    }
+    __syncthreads();
+    attn_stamp_at(rec, 7);
+
+    // p_t = s_t * inv (tp_llama.cpp:680), per head contiguous
+    {
+        const float4 iv = *reinterpret_cast<const float4 *>(hinv);
+        for (int t = tid; t < n; t += kAttnThreads) {
+            const float4 s = e[t];
+            pv[t] = __fmul_rn(s.x, iv.x);
+            if (G > 1) pv[p.stride + t] = __fmul_rn(s.y, iv.y);
+            if (G > 2) pv[2 * p.stride + t] = __fmul_rn(s.z, iv.z);
+            if (G > 3) pv[3 * p.stride + t] = __fmul_rn(s.w, iv.w);
+        }
+    }
+    if (!wait_stage(&bars[0], 0u, p.status)) atomicExch(&s_fail, 1);
+    __syncthreads();  // every p written, this CTA's V^T columns landed
+    attn_stamp_at(rec, 2);
+
+    // output chains (tp_llama.cpp:667-687): thread (column c0 + j, head h),
+    // acc = fma(v[t][c], p_t, acc) for t = 0..n-1 in order
+    const int j = tid % CW, h = tid / CW;
+    if (h < G && !s_fail) {
+        const uint8_t *vc = vt + j * S.col_stride;
+        const float *ph = pv + h * p.stride;
+        const int full = n / kPer * kPer;
+        float acc = 0.0f;
+        int t = 0;
+#pragma unroll 4
+        for (; t < full; t += kPer) {
+            const uint4 vr = *reinterpret_cast<const uint4 *>(vc + t * ESZ);
+            float v[8];
+            attn_seg_floats<ESZ>(vr, v);
+#pragma unroll
+            for (int k4 = 0; k4 < kPer; k4 += 4) {
+                const float4 p4 = *reinterpret_cast<const float4 *>(ph + t + k4);
+                acc = __fmaf_rn(v[k4], p4.x, acc);
+                acc = __fmaf_rn(v[k4 + 1], p4.y, acc);
+                acc = __fmaf_rn(v[k4 + 2], p4.z, acc);
+                acc = __fmaf_rn(v[k4 + 3], p4.w, acc);
+            }
+        }
+        for (; t < n; ++t) acc = __fmaf_rn(attn_elem<ESZ>(vc, t), ph[t], acc);
+        p.out[(static_cast<size_t>(kvh) * G + h) * D + c0 + j] = acc;
+    }
+    if (s_fail) {
+        // a copy wait ran out: let this CTA's copies in flight land (each
+        // wait bounded) before its shared memory goes away
+        if (tid == 0) {
+            if (krows) (void)wait_stage(&bars[1], 0u, p.status);
+            (void)wait_stage(&bars[0], 0u, p.status);
+        }
+        __syncthreads();
+    }
     if (rec) {
-        named_sync(1, kAttnThreads);
+        __syncthreads();
         attn_stamp_at(rec, 3);
     }
 }
@@ -87,9 +337,7 @@ AttnFn pick_attn(int d, int kv_f16) {
 int attn_kv_stride(int ctx_max) { return (ctx_max + 7) / 8 * 8; }
 
 int attn_smem_bytes(int head_dim, int kv_f16, int ctx_max) {
-    const int esz = kv_f16 ? 2 : 4;
-    return 128 + attn_core_smem_bytes(head_dim, esz, attn_colb(head_dim), attn_kc(head_dim, esz), kAttnThreads,
-                                      attn_kv_stride(ctx_max));
+    return attn_smem_layout(head_dim, kv_f16 ? 2 : 4, attn_kv_stride(ctx_max)).total;
 }
 
 int attn_launch(const AttnLaunch &L, cudaStream_t stream) {
@@ -116,15 +364,19 @@ int attn_launch(const AttnLaunch &L, cudaStream_t stream) {
     p.scale = L.scale;
     p.trace = L.trace;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(L.kvh_local);
+    cfg.gridDim = dim3(L.kvh_local * kSplit);
     cfg.blockDim = dim3(kAttnThreads);
     cfg.dynamicSmemBytes = static_cast<size_t>(smem);
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;  // kSplit CTAs of one KV head, scheduled together
+    attr[0].val.clusterDim.x = kSplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = L.pdl ? 1 : 0;
+    cfg.numAttrs = L.pdl ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, fn, p) == cudaSuccess ? 0 : kErrCuda;
 }
 
