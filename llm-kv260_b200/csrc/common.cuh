@@ -49,8 +49,21 @@ __device__ __forceinline__ int q8_quant_block(const float4 v[8], int mode, uint3
     return sum;
 }
 
-// x into shared memory for the whole CTA: int8[k] at xs, then (float32 d,
-// int32 sum of the 32 int8) per block at xs + k. `x` is float32[k] (quantised
+// Staged x in shared memory: block b's 32 int8 at xs + 48 * b (16 bytes of
+// padding each, so the blocks of 8 consecutive lanes -- what a quarter warp
+// reads in one 16-byte load -- fall in 8 different bank groups), then
+// (float32 d, int32 sum of the 32 int8) per block at xs_scales.
+constexpr int kXsBlockStride = 48;
+__host__ __device__ constexpr int xs_qbytes(int k) { return k / 32 * kXsBlockStride; }
+__host__ __device__ constexpr int xs_bytes(int k) { return xs_qbytes(k) + 8 * (k / 32); }
+__device__ __forceinline__ uint8_t *xs_block(uint8_t *xs, int b) { return xs + kXsBlockStride * b; }
+__device__ __forceinline__ const uint8_t *xs_block(const uint8_t *xs, int b) { return xs + kXsBlockStride * b; }
+__device__ __forceinline__ int2 *xs_scales(uint8_t *xs, int k) { return reinterpret_cast<int2 *>(xs + xs_qbytes(k)); }
+__device__ __forceinline__ const int2 *xs_scales(const uint8_t *xs, int k) {
+    return reinterpret_cast<const int2 *>(xs + xs_qbytes(k));
+}
+
+// x into shared memory for the whole CTA in that layout. `x` is float32[k] (quantised
 // here, q4_0.py:83-97) or the engine buffer int8[k] + float32[k/32].
 // One thread per block, all loads issued before any use and no shuffles, so
 // the staging costs one memory round trip plus one block's arithmetic; the
@@ -59,7 +72,7 @@ template <int XMODE>
 __device__ __forceinline__ void stage_x(const void *x, int k, int round_mode, uint8_t *xs) {
     const int nb = k / kQK, b = threadIdx.x;
     if (b >= nb) return;
-    uint4 *qdst = reinterpret_cast<uint4 *>(xs + 32 * b);
+    uint4 *qdst = reinterpret_cast<uint4 *>(xs_block(xs, b));
     if constexpr (XMODE == kXF32) {
         const float4 *src = reinterpret_cast<const float4 *>(x) + 8 * b;
         float4 v[8];
@@ -70,7 +83,7 @@ __device__ __forceinline__ void stage_x(const void *x, int k, int round_mode, ui
         const int sum = q8_quant_block(v, round_mode, q, &d);
         qdst[0] = make_uint4(q[0], q[1], q[2], q[3]);
         qdst[1] = make_uint4(q[4], q[5], q[6], q[7]);
-        reinterpret_cast<int2 *>(xs + k)[b] = make_int2(__float_as_int(__half2float(__float2half_rn(d))), sum);
+        xs_scales(xs, k)[b] = make_int2(__float_as_int(__half2float(__float2half_rn(d))), sum);
     } else {
         const uint8_t *xq = static_cast<const uint8_t *>(x);
         const uint4 a = __ldg(reinterpret_cast<const uint4 *>(xq + 32 * b));
@@ -87,7 +100,7 @@ __device__ __forceinline__ void stage_x(const void *x, int k, int round_mode, ui
         sum = __dp4a(static_cast<int>(c.w), 0x01010101, sum);
         qdst[0] = a;
         qdst[1] = c;
-        reinterpret_cast<int2 *>(xs + k)[b] = make_int2(__float_as_int(d), sum);
+        xs_scales(xs, k)[b] = make_int2(__float_as_int(d), sum);
     }
 }
 
@@ -100,9 +113,9 @@ struct XBlock {
 };
 
 __device__ __forceinline__ void load_xblock_smem(const uint8_t *xs, int k, int b, XBlock &xb) {
-    const uint4 a = reinterpret_cast<const uint4 *>(xs + 32 * b)[0];
-    const uint4 c = reinterpret_cast<const uint4 *>(xs + 32 * b)[1];
-    const int2 ds = reinterpret_cast<const int2 *>(xs + k)[b];
+    const uint4 a = reinterpret_cast<const uint4 *>(xs_block(xs, b))[0];
+    const uint4 c = reinterpret_cast<const uint4 *>(xs_block(xs, b))[1];
+    const int2 ds = xs_scales(xs, k)[b];
     xb.q[0] = a.x; xb.q[1] = a.y; xb.q[2] = a.z; xb.q[3] = a.w;
     xb.q[4] = c.x; xb.q[5] = c.y; xb.q[6] = c.z; xb.q[7] = c.w;
     xb.d = __int_as_float(ds.x);

@@ -410,7 +410,7 @@ int make_plan(const GemvLaunch &L, const Tuning &tu, bool encode, Plan *out) {
     p.round_mode = L.round_mode;
     p.l2_policy = L.l2_policy;
     p.groups_per_region = (p.rows_per_region + kGroupRows - 1) / kGroupRows;
-    p.xarea_bytes = round_up(L.k + 8 * nb, 16);
+    p.xarea_bytes = round_up(xs_bytes(L.k), 16);
     int cps = tu.stage_bytes / kChunkRowsBytes;
     if (cps < 1) cps = 1;
     if (cps > nch) cps = nch;

@@ -215,18 +215,19 @@ __device__ __forceinline__ void stage_x_f32(const TileParams &p, uint8_t *xs, fl
     for (int off = 1; off < TPB; off <<= 1) sum += __shfl_xor_sync(kFullMask, sum, off);
     if (live) {
         if constexpr (E == 8) {
-            *reinterpret_cast<uint2 *>(xs + i0) = make_uint2(qw[0], qw[1]);
+            *reinterpret_cast<uint2 *>(xs_block(xs, b) + E * r) = make_uint2(qw[0], qw[1]);
         } else {
 #pragma unroll
             for (int j = 0; j < E / 16; ++j)
-                reinterpret_cast<uint4 *>(xs + i0)[j] = make_uint4(qw[4 * j], qw[4 * j + 1], qw[4 * j + 2], qw[4 * j + 3]);
+                reinterpret_cast<uint4 *>(xs_block(xs, b) + E * r)[j] =
+                    make_uint4(qw[4 * j], qw[4 * j + 1], qw[4 * j + 2], qw[4 * j + 3]);
         }
-        if (r == 0) reinterpret_cast<int2 *>(xs + k)[b] = make_int2(__float_as_int(__half2float(__float2half_rn(db))), sum);
+        if (r == 0) xs_scales(xs, k)[b] = make_int2(__float_as_int(__half2float(__float2half_rn(db))), sum);
     }
 }
 
 // Byte offset of the decoder's x copy (xf) after the staged x, and its size.
-__host__ __device__ constexpr int xarea_bytes(int k) { return (k + 8 * (k / kQK) + 15) / 16 * 16; }
+__host__ __device__ constexpr int xarea_bytes(int k) { return (xs_bytes(k) + 15) / 16 * 16; }
 constexpr int norm_extra_bytes(int k) { return 4 * k + 32 * 8; }  // xf [k] floats + 32 doubles
 
 // (value desc, index asc); NaN never beats a number (the scan's rule for any
@@ -359,6 +360,22 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
         slot_off = static_cast<uint64_t>(epoch & 1u) * kMaxDecodeRanks * p.dec.slot_words;
     }
 
+    // the epilogue's global inputs for this thread's first row group, fetched
+    // now so that their latency hides behind the block math
+    const int row0 = (g0 + quad) * kTileRows + i;
+    float pre_res = 0.0f, pre_c = 0.0f, pre_s = 0.0f;
+    if constexpr (EPI == kEpiResidual) {
+        if (!xchg && l == 0 && quad < nst && row0 < p.rows) pre_res = __ldcg(p.dec.res + row0);
+    }
+    if constexpr (EPI == kEpiRopeKv) {
+        if (l == 0 && quad < nst && row0 < p.dec.q_rows + p.dec.kv_rows) {
+            const int hd = p.dec.head_dim, j = (row0 % hd) >> 1;
+            const float *cs = p.dec.rope_cs + static_cast<size_t>(dpos) * hd;
+            pre_c = __ldg(cs + 2 * j);
+            pre_s = __ldg(cs + 2 * j + 1);
+        }
+    }
+
     float best_v = __int_as_float(0x7fc00000);  // NaN: loses to any number
     int best_i = 0x7fffffff;
     bool ok = true;
@@ -410,7 +427,8 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
                     const int j = (row % hd) >> 1;
                     const float *cs = p.dec.rope_cs + static_cast<size_t>(dpos) * hd;
                     const bool even = !(row & 1);
-                    out = rope_pair(even ? yv : other, even ? other : yv, cs[2 * j], cs[2 * j + 1], even);
+                    const float c = s == quad ? pre_c : cs[2 * j], sn = s == quad ? pre_s : cs[2 * j + 1];
+                    out = rope_pair(even ? yv : other, even ? other : yv, c, sn, even);
                 }
                 p.y[row] = out;
                 if (row >= k0) {
@@ -437,7 +455,7 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
         } else if (live) {  // kEpiResidual
             if (p.y) p.y[row] = yv;
             if (!xchg) {
-                p.dec.res[row] = __fadd_rn(p.dec.res[row], yv);
+                p.dec.res[row] = __fadd_rn(s == quad ? pre_res : p.dec.res[row], yv);
             } else {
                 const uint64_t word = (static_cast<uint64_t>(epoch) << 32) | __float_as_uint(yv);
                 const uint64_t at = slot_off + static_cast<uint64_t>(p.dec.rank) * p.dec.slot_words + row;

@@ -216,10 +216,10 @@ __device__ __forceinline__ void quant_group(const float *v, bool active, int b, 
 #pragma unroll
     for (int off = 1; off < TPB; off <<= 1) sum += __shfl_xor_sync(kFullMask, sum, off);
     if (!active) return;
-    uint32_t *dst = reinterpret_cast<uint32_t *>(xs + 32 * b + j * V);
+    uint32_t *dst = reinterpret_cast<uint32_t *>(xs_block(xs, b) + j * V);
 #pragma unroll
     for (int i = 0; i < V / 4; ++i) dst[i] = w[i];
-    if (j == 0) reinterpret_cast<int2 *>(xs + k)[b] = make_int2(__float_as_int(__half2float(__float2half_rn(db))), sum);
+    if (j == 0) xs_scales(xs, k)[b] = make_int2(__float_as_int(__half2float(__float2half_rn(db))), sum);
 }
 
 template <int NWG, int TPB>
@@ -822,7 +822,7 @@ int make_params(const TokenArgs &a, MkParams *out, int *smem_bytes, int *wgs_out
     // the pick, attention buffers and scores
     MkParams q = p;
     off = 0;
-    q.off_xs = carve(kmax + 8 * (kmax / kQK));
+    q.off_xs = carve(xs_bytes(kmax));
     q.off_xf = carve(4 * a.n_embd);
     q.off_dred = carve(32 * 8);
     q.off_red = carve(wgs * 2 * kMaxBatch * 128 * 4);
