@@ -91,6 +91,7 @@ struct b200_decoder {
     uint8_t *token_embd, *lm_head;
     float *output_norm;
     float *res, *qkv_y, *attn, *act, *logits, *rope_cs;
+    uint8_t *act_q8;    // act as the down GEMV's packed x: int8[down_k] then float32 scale per 32
     int *tokens;
     DevState *st;
     void *sel_scratch;
@@ -273,10 +274,15 @@ int enqueue_token(b200_decoder_t *d) {
         norm_prologue(d, G, kProRmsnorm, W.ffn_norm);
         G.dec.epi = kEpiSiluPairs;
         G.dec.act = d->act;
+        // gate|up also writes act as the down GEMV's packed x, when its row
+        // groups still fill the GPU in the whole 4-group units that needs
+        const bool act_q8 = 2 * d->ff_rows / kTileRows / 4 >= sm_count() / 2;
+        if (act_q8) G.dec.act_q8 = d->act_q8;
         G.trace = launch_trace(d, 5 * l + 3);
         if (int rc = launch(d, G, "gate|up")) return rc;
 
-        TileLaunch D = gemv_base(d, W.down, e, d->down_k, d->act, nullptr);
+        TileLaunch D = gemv_base(d, W.down, e, d->down_k, act_q8 ? static_cast<const void *>(d->act_q8) : d->act, nullptr);
+        if (act_q8) D.xmode = kXPacked;  // quantised by the gate|up CTAs (the same Q8_0 arithmetic)
         residual_epilogue(d, D, 2 * l + 1);
         D.trace = launch_trace(d, 5 * l + 4);
         if (int rc = launch(d, D, "down")) return rc;
@@ -573,6 +579,7 @@ extern "C" int b200_decoder_create(b200_decoder_t **out, const b200_decoder_conf
     if (!rc) rc = dalloc(d, &d->qkv_y, 4 * static_cast<size_t>(d->q_rows + 2 * d->kv_rows));
     if (!rc) rc = dalloc(d, &d->attn, 4 * static_cast<size_t>(o_k));
     if (!rc) rc = dalloc(d, &d->act, 4 * static_cast<size_t>(down_k));
+    if (!rc) rc = dalloc(d, &d->act_q8, static_cast<size_t>(down_k) + 4 * static_cast<size_t>(down_k / kQK));
     if (!rc) rc = dalloc(d, &d->logits, 4 * static_cast<size_t>(d->vocab_rows));
     if (!rc) rc = dalloc(d, &d->rope_cs, 4 * static_cast<size_t>(c.ctx_max) * c.head_dim);
     if (!rc) rc = dalloc(d, &d->tokens, 4 * (static_cast<size_t>(c.ctx_max) + 1));

@@ -129,6 +129,9 @@ struct DecodeOps {
     void *kcache = nullptr;            // this layer's K cache [kv head][kv_stride][head_dim]
     void *vcache = nullptr;            // and V^T cache [kv head][head_dim][kv_stride]
     float *act = nullptr;              // kEpiSiluPairs output [rows / 2]
+    uint8_t *act_q8 = nullptr;         // kEpiSiluPairs, optional: act also as packed x for the next GEMV --
+                                       // int8[rows / 2] then float32 scale per 32 (q4_0.py:193-200); the row
+                                       // groups are then split over CTAs in units of 4 (whole 32-value blocks)
     int nranks = 1, rank = 0;          // kEpiResidual across ranks:
     uint64_t *win_words[kMaxDecodeRanks] = {};  // every rank's word area as mapped here, [slot][source rank][row]
     uint64_t slot_words = 0;           // words per (slot, source rank)

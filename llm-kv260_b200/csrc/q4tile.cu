@@ -50,6 +50,8 @@ struct TileParams {
     unsigned *status;
     int rows, k, nb, nch;
     int groups;
+    int unit;        // row groups are split over CTAs in whole units of this many groups
+    int act_off;     // kEpiSiluPairs with act_q8: byte offset of the CTA's act values after xs
     int slot_bytes;  // nch * 2304: one row group
     int stages;
     int round_mode;
@@ -238,6 +240,30 @@ __device__ __forceinline__ bool sel_better(float av, int ai, float bv, int bi) {
     return av > bv || (av == bv && ai < bi);
 }
 
+// Q8_0 of a CTA's act values (its row groups [g0, g1) give act values
+// [8 g0, 8 g1): whole 32-value blocks) into the packed x at p.dec.act_q8:
+// int8 at byte 32 b, then the float16-rounded scale as float32 at K + 4 b
+// (K = rows / 2) -- the engine's buffer (q4_0.py:193-200), which the next
+// GEMV stages with the packed path. One warp per block, one value per lane;
+// the block maximum meets by xor shuffles (fmaxf does not depend on the
+// order); the rest is q8_quant_block's arithmetic (q4_0.py:83-97). Called
+// by every consumer warp; `ok` must be uniform within each warp.
+__device__ __forceinline__ void quantize_act_blocks(const TileParams &p, const float *vals, int g0, int g1, bool ok) {
+    const int K = p.rows / 2, lane = threadIdx.x & 31;
+    const int b0 = g0 * (kTileRows / 2) / kQK, nblk = (g1 - g0) * (kTileRows / 2) / kQK;
+    if (!ok) return;
+    for (int bl = threadIdx.x >> 5; bl < nblk; bl += kConsumers / 32) {
+        const float v = vals[bl * kQK + lane];
+        float am = fabsf(v);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(kFullMask, am, off));
+        const float db = __fdiv_rn(am, 127.0f);
+        const float inv = db == 0.0f ? 0.0f : __fdiv_rn(1.0f, db);
+        p.dec.act_q8[kQK * (b0 + bl) + lane] = static_cast<uint8_t>(q8_round(__fmul_rn(v, inv), p.round_mode) & 0xff);
+        if (lane == 0) reinterpret_cast<float *>(p.dec.act_q8 + K)[b0 + bl] = __half2float(__float2half_rn(db));
+    }
+}
+
 // Block term of one chunk-tile for row i, lane l.
 __device__ __forceinline__ float tile_term(const uint8_t *tile, int i, int l, const XBlock &xb) {
     const int u = i * kLanes + l;
@@ -282,8 +308,9 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
     uint8_t *xs = ring + p.stages * p.slot_bytes;
 
     const int t = threadIdx.x, warp = t / 32, lane = t % 32;
-    const int g0 = static_cast<int>(static_cast<long long>(p.groups) * blockIdx.x / gridDim.x);
-    const int g1 = static_cast<int>(static_cast<long long>(p.groups) * (blockIdx.x + 1) / gridDim.x);
+    const int units = (p.groups + p.unit - 1) / p.unit;
+    const int g0 = min(p.groups, p.unit * static_cast<int>(static_cast<long long>(units) * blockIdx.x / gridDim.x));
+    const int g1 = min(p.groups, p.unit * static_cast<int>(static_cast<long long>(units) * (blockIdx.x + 1) / gridDim.x));
     const int S = p.stages, nst = g1 - g0;
 
     if (t == 0) {
@@ -450,7 +477,11 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
             const float other = __shfl_xor_sync(kFullMask, yv, 8);
             if (live) {
                 if (p.y) p.y[row] = yv;
-                if (!(row & 1)) p.dec.act[row >> 1] = silu_mul(yv, other);
+                if (!(row & 1)) {
+                    const float a = silu_mul(yv, other);
+                    p.dec.act[row >> 1] = a;
+                    if (p.dec.act_q8) reinterpret_cast<float *>(xs + p.act_off)[(row >> 1) - g0 * (kTileRows / 2)] = a;
+                }
             }
         } else if (live) {  // kEpiResidual
             if (p.y) p.y[row] = yv;
@@ -464,6 +495,14 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
         }
     }
     trace_stamp(p.trace, 5);
+    if constexpr (EPI == kEpiSiluPairs) {
+        if (p.dec.act_q8) {
+            // this CTA's act values as whole Q8_0 blocks of the next GEMV's
+            // packed x (q4_0.py:83-97, 193-200)
+            named_sync(1, kConsumers);
+            quantize_act_blocks(p, reinterpret_cast<const float *>(xs + p.act_off), g0, g1, __all_sync(kFullMask, ok));
+        }
+    }
     if (xchg && ok && l == 0) {
         // Every rank computed these rows' partials for its K slice; collect
         // them from this rank's window and sum in rank order
@@ -611,6 +650,8 @@ TileKernelFn pick_tile(int xmode, bool xreg, int pro, int epi, bool pick) {
                                            : tile_fn<kXPacked, kProPlain, kEpiStore, false>(xreg);
         return pick ? tile_fn<kXF32, kProPlain, kEpiStore, true>(xreg) : tile_fn<kXF32, kProPlain, kEpiStore, false>(xreg);
     }
+    if (xmode == kXPacked && pro == kProPlain && epi == kEpiResidual && !pick)
+        return tile_fn<kXPacked, kProPlain, kEpiResidual, false>(xreg);
     if (xmode != kXF32) return nullptr;
     if (pro == kProEmbedNorm && epi == kEpiRopeKv && !pick) return tile_fn<kXF32, kProEmbedNorm, kEpiRopeKv, false>(xreg);
     if (pro == kProRmsnorm && epi == kEpiRopeKv && !pick) return tile_fn<kXF32, kProRmsnorm, kEpiRopeKv, false>(xreg);
@@ -646,6 +687,8 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
     p.nb = nb;
     p.nch = nch;
     p.groups = (L.rows + kTileRows - 1) / kTileRows;
+    p.unit = L.dec.act_q8 ? 4 : 1;
+    const int units = (p.groups + p.unit - 1) / p.unit;
     p.slot_bytes = nch * kTileBytes;
     p.round_mode = L.round_mode;
     p.l2_policy = L.l2_policy;
@@ -658,7 +701,16 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
     }
     p.dec = L.dec;
     p.trace = L.trace;
-    const int xarea = xarea_bytes(L.k) + (L.dec.pro != kProPlain ? norm_extra_bytes(L.k) : 0);
+    int xarea = xarea_bytes(L.k) + (L.dec.pro != kProPlain ? norm_extra_bytes(L.k) : 0);
+    if (L.dec.act_q8) {
+        // the CTA's act values: at most ceil(units / min(SMs, units)) units
+        // (the grid is at least that large)
+        const int sms0 = sm_count();
+        if (sms0 <= 0) return kErrNoDev;
+        const int gmin = units < sms0 ? units : sms0;
+        p.act_off = xarea;
+        xarea += (units + gmin - 1) / gmin * p.unit * (kTileRows / 2) * 4;
+    }
     const int fixed = kSmemAlign + xarea;
     const int limit = max_smem_optin() - 1024;  // static shared memory
     int stages = tu.stages < 1 ? 1 : (tu.stages > kMaxStages ? kMaxStages : tu.stages);
@@ -673,7 +725,7 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
     if (fit < 1) return kErrInval;
     if (per_sm > fit) per_sm = fit;  // one wave: every CTA resident at once
     int grid = sms * per_sm;
-    if (grid > p.groups) grid = p.groups;
+    if (grid > units) grid = units;
     if (grid > kSelMaxCtas) grid = kSelMaxCtas;
     out->p = p;
     out->fn = fn;
@@ -721,6 +773,8 @@ int tile_validate(const TileLaunch &L, const char **why) {
             return bad("rope/KV epilogue: inconsistent q/k/v rows, head_dim or caches");
     }
     if (D.epi == kEpiSiluPairs && (!D.act || L.rows % 2)) return bad("silu epilogue: act needed, rows even");
+    if (D.act_q8 && (D.epi != kEpiSiluPairs || L.rows % 64 || reinterpret_cast<uintptr_t>(D.act_q8) % 16))
+        return bad("act_q8: a SiLU epilogue over whole 32-value blocks, 16-byte aligned");
     if (D.epi == kEpiResidual) {
         if (!D.res) return bad("residual epilogue: res needed");
         if (D.nranks < 1 || D.nranks > kMaxDecodeRanks || D.rank < 0 || D.rank >= D.nranks)
