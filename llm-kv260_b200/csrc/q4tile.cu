@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
         if constexpr (XREG) {
             stage_x_f32<4, PRO>(p, xs, xf, dred);
         } else {
-            if (stage_tpb(p.nb) == 2)
+            if (p.nb * 2 <= kConsumers)
                 stage_x_f32<2, PRO>(p, xs, xf, dred);
             else
                 stage_x_f32<1, PRO>(p, xs, xf, dred);
@@ -713,8 +713,14 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
     }
     const int fixed = kSmemAlign + xarea;
     const int limit = max_smem_optin() - 1024;  // static shared memory
-    int stages = tu.stages < 1 ? 1 : (tu.stages > kMaxStages ? kMaxStages : tu.stages);
-    while (stages > 1 && fixed + stages * p.slot_bytes > limit) stages -= 1;
+    // A quad waits for a stage by its mbarrier's phase parity, which names
+    // the right fill only while the stage's previous group was the same
+    // quad's: the quads take groups round-robin, so the stage count is a
+    // multiple of kQuads (with 1 or 3 stages and 2 quads, a quad could pass
+    // the wait for its next group on the previous fill and read stale tiles).
+    int stages = tu.stages < kQuads ? kQuads : (tu.stages > kMaxStages ? kMaxStages : tu.stages);
+    stages -= stages % kQuads;
+    while (stages > kQuads && fixed + stages * p.slot_bytes > limit) stages -= kQuads;
     p.stages = stages;
     const int smem = fixed + stages * p.slot_bytes;
     if (smem > limit) return kErrInval;

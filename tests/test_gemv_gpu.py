@@ -146,6 +146,20 @@ def test_pipeline_shapes_do_not_change_bits(torch_mod, pkg, eng, oracle, stage_b
     assert np.array_equal(_bits(got), _bits(want))
 
 
+@pytest.mark.parametrize("k", [2048, 8192])
+@pytest.mark.parametrize("stages", [1, 3, 5])
+def test_many_groups_per_cta_with_odd_stage_requests(torch_mod, pkg, eng, oracle, stages, k):
+    """Tile layout, one CTA per SM and at least 6 row groups per CTA: the ring
+    wraps several times for each consumer quad, whatever stage count is asked."""
+    rows = 16 * 148 * 6 + 5
+    blocks = oracle.quantize_q4_0(cases.std_weights(rows, k, 77 + stages))
+    x = cases.std_weights(1, k, 78)[0]
+    want = oracle.gemv_q4_0_f32(blocks, k, x)
+    for fuse in (0, 1):
+        got = _run_engine(torch_mod, pkg, eng, blocks, k, x, fuse=fuse, stages=stages, ctas_per_sm=1, layout=1)
+        assert np.array_equal(_bits(got), _bits(want)), (stages, fuse)
+
+
 def test_zero_and_degenerate_activations(torch_mod, pkg, eng, oracle):
     """All-zero x (d = 0, inv = 0), negative zeros, tiny values, zero weight blocks."""
     k = 512
