@@ -107,7 +107,9 @@ constexpr int kMaxDecodeRanks = 8;
 // 0 after the CTA's set-up, 1 when the previous kernel's results are visible
 // (griddepcontrol.wait returned), 2 when its input is staged (attention: p
 // computed), 3 at its end; the tile GEMV also 4 its first weight stage
-// landed, 5 its row groups done (thread 0's quad); attention 4 q staged,
+// landed, 5 its row groups done (thread 0's quad), with an RMSNorm prologue
+// 6 the sum of squares' warp reduction done and 7 the norm scale known;
+// attention 4 q staged,
 // 5 scores and maxima, 6 exponentials, 7 sums, 8 + 2c / 9 + 2c V^T chunk c
 // (< 4) landed / consumed.
 constexpr int kTraceCtas = 1024;

@@ -84,10 +84,6 @@ __device__ __forceinline__ uint64_t ld_word(const uint64_t *p) {
     return w;
 }
 
-// Threads per 32-block when staging a float32 x: 4, 2 or 1, as many as the
-// consumers allow for k/32 blocks.
-__device__ __forceinline__ int stage_tpb(int nb) { return nb * 4 <= kConsumers ? 4 : (nb * 2 <= kConsumers ? 2 : 1); }
-
 // RMSNorm's sequential fallback (tp_llama.cpp:560-564): lane j sums x[i]^2
 // for i = j, j+4, ... in order, threads 0-3, then (l0 + l2) + (l1 + l3);
 // returns (float)(ss / k). Out of line: rarely taken, and the hot code stays
@@ -177,6 +173,7 @@ __device__ __forceinline__ void stage_x_f32(const TileParams &p, uint8_t *xs, fl
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) ss = __dadd_rn(ss, __shfl_xor_sync(kFullMask, ss, off));
         if (lane == 0) dred[warp] = ss;
+        trace_stamp(p.trace, 6);
         if (live) {
             float4 *xd = reinterpret_cast<float4 *>(xf + i0);
 #pragma unroll
@@ -190,6 +187,7 @@ __device__ __forceinline__ void stage_x_f32(const TileParams &p, uint8_t *xs, fl
         float f = __double2float_rn(q);
         if (p.dec.exact_norm || !rms_float_is_safe(q, f, k)) f = rms_sequential(xf, dred, k);
         const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(f, p.dec.eps)));
+        trace_stamp(p.trace, 7);
 #pragma unroll
         for (int j = 0; j < E; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], scale), w[j]);
     }
