@@ -312,6 +312,11 @@ bool ensure_smem(const void *fn, int bytes) {
     for (int i = 0; i < used; ++i)
         if (cache[i].fn == fn && cache[i].dev == dev && cache[i].bytes >= bytes) return true;
     if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+    // every kernel asks for the same (largest) shared-memory split of the
+    // SM's on-chip memory, so CTAs of consecutive launches can share an SM
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) !=
+        cudaSuccess)
+        return false;
     if (used < 256) cache[used++] = Entry{fn, dev, bytes};
     return true;
 }

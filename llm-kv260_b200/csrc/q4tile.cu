@@ -113,8 +113,9 @@ __device__ __noinline__ float rms_sequential(const float *xf, double *dred, int 
 // block's Q8_0 quantisation (q4_0.py:83-97) meets its maximum and its int
 // sum across the block's TPB adjacent lanes by xor shuffles: the maximum
 // (fmaxf) and an integer sum do not depend on the order.
-template <int TPB, int PRO>
-__device__ __forceinline__ void stage_x_f32(const TileParams &p, uint8_t *xs, float *xf, double *dred) {
+template <int TPB, int PRO, typename AfterWait>
+__device__ __forceinline__ void stage_x_f32(const TileParams &p, uint8_t *xs, float *xf, double *dred,
+                                            AfterWait &&after_wait) {
     constexpr int E = 32 / TPB;
     const int k = p.k, nb = k / kQK, t = threadIdx.x, b = t / TPB, r = t % TPB, lane = t % 32, warp = t / 32;
     const bool live = b < nb;
@@ -134,6 +135,7 @@ __device__ __forceinline__ void stage_x_f32(const TileParams &p, uint8_t *xs, fl
     }
     pdl_wait_prior_grid();
     trace_stamp(p.trace, 1);
+    after_wait();
     float v[E];
 #pragma unroll
     for (int j = 0; j < E; ++j) v[j] = 0.0f;
@@ -294,8 +296,20 @@ __device__ __forceinline__ bool ring_wait(uint64_t *bar, uint32_t parity, unsign
 // pick) that a caller uses (pick_tile): each launch runs a compact,
 // contiguous code path -- a kernel holding every variant is several times
 // larger than an SM's instruction cache keeps across the token's launches.
+// Registers per thread, so that a launch's CTAs can start on SMs where the
+// previous launch's CTAs still run (the SM has 65536 registers): the o GEMV
+// (float32 x, plain prologue, residual epilogue) beside an attention CTA
+// (256 x 96), and the down GEMV (packed x, residual epilogue) under a q|k|v
+// GEMV CTA (288 x 128).
+template <int XMODE, int PRO, int EPI>
+struct TileRegs {
+    static constexpr int value = (XMODE == kXF32 && PRO == kProPlain && EPI == kEpiResidual)     ? 136
+                                 : (XMODE == kXPacked && PRO == kProPlain && EPI == kEpiResidual) ? 96
+                                                                                                  : 224;
+};
+
 template <int XMODE, bool XREG, int PRO, int EPI, bool PICK>
-__global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_constant__ TileParams p) {
+__global__ void __maxnreg__((TileRegs<XMODE, PRO, EPI>::value)) q4_tile_kernel(const __grid_constant__ TileParams p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t full[kMaxStages], empty[kMaxStages];
     __shared__ int s_abort;
@@ -348,59 +362,64 @@ __global__ void __launch_bounds__(kTileThreads, 1) q4_tile_kernel(const __grid_c
         return;
     }
 
+    const int quad = warp / 4, i = (warp % 4) * 4 + (lane >> 3), l = lane & 7;
+    constexpr int epi = EPI;
+    const bool xchg = epi == kEpiResidual && p.dec.nranks > 1;
+    const int row0 = (g0 + quad) * kTileRows + i;
+    int dpos = 0;
+    uint32_t epoch = 0;
+    uint64_t slot_off = 0;
+    float pre_res = 0.0f, pre_c = 0.0f, pre_s = 0.0f;
+    // The epilogue's global inputs -- the position, the exchange epoch, this
+    // thread's first residual value or RoPE pair -- are fetched as soon as
+    // the previous kernel's results are visible, so their latency (a
+    // dependent pair of loads for RoPE) hides behind the x staging.
+    auto after_wait = [&]() {
+        if constexpr (EPI == kEpiRopeKv) {
+            dpos = *p.dec.pos;
+            if (l == 0 && quad < nst && row0 < p.dec.q_rows + p.dec.kv_rows) {
+                const int hd = p.dec.head_dim, j = (row0 % hd) >> 1;
+                const float *cs = p.dec.rope_cs + static_cast<size_t>(dpos) * hd;
+                pre_c = __ldg(cs + 2 * j);
+                pre_s = __ldg(cs + 2 * j + 1);
+            }
+        }
+        if constexpr (EPI == kEpiResidual) {
+            if (xchg) {
+                epoch = *p.dec.step * static_cast<uint32_t>(p.dec.ar_per_token) + static_cast<uint32_t>(p.dec.ar_index) + 1u;
+                slot_off = static_cast<uint64_t>(epoch & 1u) * kMaxDecodeRanks * p.dec.slot_words;
+            } else if (l == 0 && quad < nst && row0 < p.rows) {
+                pre_res = __ldcg(p.dec.res + row0);
+            }
+        }
+    };
     if constexpr (XMODE == kXF32) {
         float *xf = reinterpret_cast<float *>(xs + xarea_bytes(p.k));    // with a norm prologue only
         double *dred = reinterpret_cast<double *>(xs + xarea_bytes(p.k) + 4 * p.k);
         // K <= 2048 (XREG) always stages with 4 threads per block; only the
         // variants a kernel can reach are compiled into it
         if constexpr (XREG) {
-            stage_x_f32<4, PRO>(p, xs, xf, dred);
+            stage_x_f32<4, PRO>(p, xs, xf, dred, after_wait);
         } else {
             if (p.nb * 2 <= kConsumers)
-                stage_x_f32<2, PRO>(p, xs, xf, dred);
+                stage_x_f32<2, PRO>(p, xs, xf, dred, after_wait);
             else
-                stage_x_f32<1, PRO>(p, xs, xf, dred);
+                stage_x_f32<1, PRO>(p, xs, xf, dred, after_wait);
         }
     } else {
         pdl_wait_prior_grid();
         trace_stamp(p.trace, 1);
+        after_wait();
         stage_x<XMODE>(p.x, p.k, p.round_mode, xs);
     }
     named_sync(1, kConsumers);
     trace_stamp(p.trace, 2);
-    const int quad = warp / 4, i = (warp % 4) * 4 + (lane >> 3), l = lane & 7;
     XBlock xr[XREG ? kXregChunks : 1];
     if constexpr (XREG) {
 #pragma unroll
         for (int c = 0; c < kXregChunks; ++c)
             if (c < p.nch) load_xblock_smem(xs, p.k, 8 * c + l, xr[c]);
     }
-    constexpr int epi = EPI;
-    const int dpos = (epi == kEpiRopeKv) ? *p.dec.pos : 0;
-    const bool xchg = epi == kEpiResidual && p.dec.nranks > 1;
-    uint32_t epoch = 0;
-    uint64_t slot_off = 0;
-    if (xchg) {
-        epoch = *p.dec.step * static_cast<uint32_t>(p.dec.ar_per_token) + static_cast<uint32_t>(p.dec.ar_index) + 1u;
-        slot_off = static_cast<uint64_t>(epoch & 1u) * kMaxDecodeRanks * p.dec.slot_words;
-    }
-
-    // the epilogue's global inputs for this thread's first row group, fetched
-    // now so that their latency hides behind the block math
-    const int row0 = (g0 + quad) * kTileRows + i;
-    float pre_res = 0.0f, pre_c = 0.0f, pre_s = 0.0f;
-    if constexpr (EPI == kEpiResidual) {
-        if (!xchg && l == 0 && quad < nst && row0 < p.rows) pre_res = __ldcg(p.dec.res + row0);
-    }
-    if constexpr (EPI == kEpiRopeKv) {
-        if (l == 0 && quad < nst && row0 < p.dec.q_rows + p.dec.kv_rows) {
-            const int hd = p.dec.head_dim, j = (row0 % hd) >> 1;
-            const float *cs = p.dec.rope_cs + static_cast<size_t>(dpos) * hd;
-            pre_c = __ldg(cs + 2 * j);
-            pre_s = __ldg(cs + 2 * j + 1);
-        }
-    }
-
     float best_v = __int_as_float(0x7fc00000);  // NaN: loses to any number
     int best_i = 0x7fffffff;
     bool ok = true;
@@ -711,26 +730,41 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
     }
     const int fixed = kSmemAlign + xarea;
     const int limit = max_smem_optin() - 1024;  // static shared memory
-    // A quad waits for a stage by its mbarrier's phase parity, which names
-    // the right fill only while the stage's previous group was the same
-    // quad's: the quads take groups round-robin, so the stage count is a
-    // multiple of kQuads (with 1 or 3 stages and 2 quads, a quad could pass
-    // the wait for its next group on the previous fill and read stale tiles).
-    int stages = tu.stages < kQuads ? kQuads : (tu.stages > kMaxStages ? kMaxStages : tu.stages);
-    stages -= stages % kQuads;
-    while (stages > kQuads && fixed + stages * p.slot_bytes > limit) stages -= kQuads;
-    p.stages = stages;
-    const int smem = fixed + stages * p.slot_bytes;
-    if (smem > limit) return kErrInval;
     const int sms = sm_count();
     if (sms <= 0) return kErrNoDev;
+    const int cap = tu.stages < 1 ? 1 : (tu.stages > kMaxStages ? kMaxStages : tu.stages);
+    // The grid decides how many row groups the busiest CTA takes (`need`),
+    // and so how many stages are worth their shared memory (a small ring
+    // leaves room on the SM for the next launch's CTA); that memory in turn
+    // decides how many CTAs fit on an SM. Start from the asked CTAs per SM
+    // and step down until they fit.
     int per_sm = tu.ctas_per_sm < 1 ? 1 : tu.ctas_per_sm;
-    const int fit = resident_ctas(reinterpret_cast<const void *>(fn), kTileThreads, smem);
-    if (fit < 1) return kErrInval;
-    if (per_sm > fit) per_sm = fit;  // one wave: every CTA resident at once
-    int grid = sms * per_sm;
-    if (grid > units) grid = units;
-    if (grid > kSelMaxCtas) grid = kSelMaxCtas;
+    int grid = 0, stages = 0, smem = 0;
+    for (;;) {
+        grid = sms * per_sm;
+        if (grid > units) grid = units;
+        if (grid > kSelMaxCtas) grid = kSelMaxCtas;
+        const int need = (units + grid - 1) / grid * p.unit;
+        if (need <= cap && fixed + need * p.slot_bytes <= limit) {
+            stages = need;  // every group its own stage: no stage is filled twice
+        } else {
+            // A quad waits for a stage by its mbarrier's phase parity, which
+            // names the right fill only while the stage's previous group was
+            // the same quad's: the quads take groups round-robin, so a stage
+            // count that refills stages is a multiple of kQuads (with 1 or 3
+            // stages and 2 quads, a quad could pass the wait for its next
+            // group on the previous fill and read stale tiles).
+            stages = cap < kQuads ? kQuads : cap - cap % kQuads;
+            while (stages > kQuads && fixed + stages * p.slot_bytes > limit) stages -= kQuads;
+        }
+        smem = fixed + stages * p.slot_bytes;
+        if (smem > limit) return kErrInval;
+        const int fit = resident_ctas(reinterpret_cast<const void *>(fn), kTileThreads, smem);
+        if (fit < 1) return kErrInval;
+        if (per_sm <= fit) break;  // one wave: every CTA resident at once
+        per_sm = fit;
+    }
+    p.stages = stages;
     out->p = p;
     out->fn = fn;
     out->grid = grid;
