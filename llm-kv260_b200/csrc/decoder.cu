@@ -279,6 +279,7 @@ int enqueue_token(b200_decoder_t *d) {
         const bool act_q8 = 2 * d->ff_rows / kTileRows / 4 >= sm_count() / 2;
         if (act_q8) G.dec.act_q8 = d->act_q8;
         G.trace = launch_trace(d, 5 * l + 3);
+        G.max_stages = 4;  // a ring small enough for a down GEMV CTA to start beside it
         if (int rc = launch(d, G, "gate|up")) return rc;
 
         TileLaunch D = gemv_base(d, W.down, e, d->down_k, act_q8 ? static_cast<const void *>(d->act_q8) : d->act, nullptr);

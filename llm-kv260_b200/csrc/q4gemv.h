@@ -162,6 +162,7 @@ struct TileLaunch {
     void *sel_scratch = nullptr;  // tile_select_scratch_bytes(), ticket zeroed once
     DecodeOps dec;                // decoder prologue/epilogue (plain GEMV by default)
     uint64_t *trace = nullptr;    // optional: [CTA < kTraceCtas][kTraceStamps] global-timer stamps
+    int max_stages = 0;           // > 0: at most this many ring stages (below Tuning::stages)
 };
 int tile_select_scratch_bytes();
 

@@ -732,7 +732,8 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
     const int limit = max_smem_optin() - 1024;  // static shared memory
     const int sms = sm_count();
     if (sms <= 0) return kErrNoDev;
-    const int cap = tu.stages < 1 ? 1 : (tu.stages > kMaxStages ? kMaxStages : tu.stages);
+    int cap = tu.stages < 1 ? 1 : (tu.stages > kMaxStages ? kMaxStages : tu.stages);
+    if (L.max_stages > 0 && L.max_stages < cap) cap = L.max_stages;
     // The grid decides how many row groups the busiest CTA takes (`need`),
     // and so how many stages are worth their shared memory (a small ring
     // leaves room on the SM for the next launch's CTA); that memory in turn
