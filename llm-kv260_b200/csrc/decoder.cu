@@ -187,6 +187,7 @@ TileLaunch gemv_base(const b200_decoder_t *d, const uint8_t *w, int rows, int k,
     L.round_mode = d->c.round_mode;
     L.l2_policy = kL2EvictFirst;
     L.pdl = true;
+    L.ring_to_groups = true;  // the next launch's CTAs start beside this one's
     return L;
 }
 

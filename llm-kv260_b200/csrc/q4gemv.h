@@ -163,6 +163,10 @@ struct TileLaunch {
     DecodeOps dec;                // decoder prologue/epilogue (plain GEMV by default)
     uint64_t *trace = nullptr;    // optional: [CTA < kTraceCtas][kTraceStamps] global-timer stamps
     int max_stages = 0;           // > 0: at most this many ring stages (below Tuning::stages)
+    // Size the ring to the busiest CTA's row groups (a small ring leaves room
+    // on the SM for the next launch's CTA: the decoder's chain of dependent
+    // launches). Off, the ring has as many stages as Tuning asks and fit.
+    bool ring_to_groups = false;
 };
 int tile_select_scratch_bytes();
 

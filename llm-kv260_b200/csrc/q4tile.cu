@@ -735,10 +735,10 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
     int cap = tu.stages < 1 ? 1 : (tu.stages > kMaxStages ? kMaxStages : tu.stages);
     if (L.max_stages > 0 && L.max_stages < cap) cap = L.max_stages;
     // The grid decides how many row groups the busiest CTA takes (`need`),
-    // and so how many stages are worth their shared memory (a small ring
-    // leaves room on the SM for the next launch's CTA); that memory in turn
-    // decides how many CTAs fit on an SM. Start from the asked CTAs per SM
-    // and step down until they fit.
+    // and with ring_to_groups how many stages are worth their shared memory
+    // (a small ring leaves room on the SM for the next launch's CTA); that
+    // memory in turn decides how many CTAs fit on an SM. Start from the
+    // asked CTAs per SM and step down until they fit.
     int per_sm = tu.ctas_per_sm < 1 ? 1 : tu.ctas_per_sm;
     int grid = 0, stages = 0, smem = 0;
     for (;;) {
@@ -746,7 +746,7 @@ int make_tile_plan(const TileLaunch &L, const Tuning &tu, TilePlan *out) {
         if (grid > units) grid = units;
         if (grid > kSelMaxCtas) grid = kSelMaxCtas;
         const int need = (units + grid - 1) / grid * p.unit;
-        if (need <= cap && fixed + need * p.slot_bytes <= limit) {
+        if (L.ring_to_groups && need <= cap && fixed + need * p.slot_bytes <= limit) {
             stages = need;  // every group its own stage: no stage is filled twice
         } else {
             // A quad waits for a stage by its mbarrier's phase parity, which
