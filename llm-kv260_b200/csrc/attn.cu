@@ -217,15 +217,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
         mx[2] = attn_max_gt(mx[2], s.z);
         mx[3] = attn_max_gt(mx[3], s.w);
     }
+    // the four heads' reductions interleaved (a head past G is never read)
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-        if (b < G) {
-            float m = mx[b];
+    for (int off = 16; off > 0; off >>= 1) {
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) m = attn_max_gt(m, __shfl_xor_sync(kFullMask, m, off));
-            if (lane == 0) part[warp * 4 + b] = m;
-        }
+        for (int b = 0; b < 4; ++b) mx[b] = attn_max_gt(mx[b], __shfl_xor_sync(kFullMask, mx[b], off));
     }
+    if (lane == 0) *reinterpret_cast<float4 *>(part + warp * 4) = make_float4(mx[0], mx[1], mx[2], mx[3]);
     __syncthreads();
     float m[4] = {-1e30f, -1e30f, -1e30f, -1e30f};
     for (int w = 0; w < kAttnThreads / 32; ++w) {
@@ -262,7 +260,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
         if (b < G && j4 == 0) {
             float sum = y;
             for (int t = n4; t < n; ++t) sum = __fadd_rn(sum, col[4 * t]);
-            hinv[b] = __fdiv_rn(1.0f, sum);
+            hinv[b] = __frcp_rn(sum);  // IEEE 1 / sum, round to nearest: the reference's 1.0f / sum
         }
     }
     __syncthreads();
