@@ -181,17 +181,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
                 float f[8];
                 attn_seg_floats<ESZ>(kr[j], f);
                 const int i0 = (s8 + j) * kPer;
+                // the segment's q of all four heads loaded together, then the
+                // FMAs (qs holds 4 heads; a head past G is computed, never used)
+                float4 qv[4][kPer / 4];
+#pragma unroll
+                for (int b = 0; b < 4; ++b)
+#pragma unroll
+                    for (int m4 = 0; m4 < kPer; m4 += 4) qv[b][m4 / 4] = *reinterpret_cast<const float4 *>(qs + b * D + i0 + m4);
 #pragma unroll
                 for (int b = 0; b < 4; ++b) {
-                    if (b < G) {
 #pragma unroll
-                        for (int m4 = 0; m4 < kPer; m4 += 4) {
-                            const float4 q4 = lds_f4(qs + b * D + i0 + m4);
-                            a[b][0] = __fmaf_rn(f[m4], q4.x, a[b][0]);
-                            a[b][1] = __fmaf_rn(f[m4 + 1], q4.y, a[b][1]);
-                            a[b][2] = __fmaf_rn(f[m4 + 2], q4.z, a[b][2]);
-                            a[b][3] = __fmaf_rn(f[m4 + 3], q4.w, a[b][3]);
-                        }
+                    for (int m4 = 0; m4 < kPer; m4 += 4) {
+                        const float4 q4 = qv[b][m4 / 4];
+                        a[b][0] = __fmaf_rn(f[m4], q4.x, a[b][0]);
+                        a[b][1] = __fmaf_rn(f[m4 + 1], q4.y, a[b][1]);
+                        a[b][2] = __fmaf_rn(f[m4 + 2], q4.z, a[b][2]);
+                        a[b][3] = __fmaf_rn(f[m4 + 3], q4.w, a[b][3]);
                     }
                 }
             }
