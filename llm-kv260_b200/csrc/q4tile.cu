@@ -433,9 +433,29 @@ __global__ void __maxnreg__((TileRegs<XMODE, PRO, EPI>::value)) q4_tile_kernel(c
         const uint8_t *tiles = ring + static_cast<size_t>(slot) * p.slot_bytes;
         float acc = 0.0f;
         if constexpr (XREG) {
+            // four chunks' tile words loaded together, then their terms in
+            // chunk order (the lane chain's order)
+            const int u = i * kLanes + l;
 #pragma unroll
-            for (int c = 0; c < kXregChunks; ++c)
-                if (c < p.nch) acc = __fadd_rn(acc, tile_term(tiles + c * kTileBytes, i, l, xr[c]));
+            for (int c0 = 0; c0 < kXregChunks; c0 += 4) {
+                uint4 nv[4];
+                uint32_t dv[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    if (c0 + c < p.nch) {
+                        const uint8_t *tile = tiles + (c0 + c) * kTileBytes;
+                        nv[c] = *reinterpret_cast<const uint4 *>(tile + u * 16);
+                        dv[c] = *reinterpret_cast<const uint16_t *>(tile + kTileNibBytes + u * 2);
+                    }
+                }
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    if (c0 + c < p.nch) {
+                        const uint32_t n[4] = {nv[c].x, nv[c].y, nv[c].z, nv[c].w};
+                        acc = __fadd_rn(acc, block_term_words(n, dv[c], xr[c0 + c]));
+                    }
+                }
+            }
         } else {
 #pragma unroll 4
             for (int c = 0; c < p.nch; ++c) {
