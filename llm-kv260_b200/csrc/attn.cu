@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
         const int full = n / kPer * kPer;
         float acc = 0.0f;
         int t = 0;
-#pragma unroll 4
+#pragma unroll 8
         for (; t < full; t += kPer) {
             const uint4 vr = *reinterpret_cast<const uint4 *>(vc + t * ESZ);
             float v[8];
