@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
         const float *col = reinterpret_cast<const float *>(e) + b;
         float acc = 0.0f;
         if (b < G) {
-#pragma unroll 8
+#pragma unroll 16
             for (int t = j4; t < n4; t += 4) acc = __fadd_rn(acc, col[4 * t]);
         }
         const float x = __fadd_rn(acc, __shfl_xor_sync(kFullMask, acc, 1));
