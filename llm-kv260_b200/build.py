@@ -9,6 +9,7 @@ public symbols are the ones declared in include/*.h.
 
 from __future__ import annotations
 
+import concurrent.futures
 import glob
 import os
 import subprocess
@@ -45,14 +46,16 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if not force and up_to_date():
         return LIB
     os.makedirs(OBJ, exist_ok=True)
-    objs = []
+    objs, cmds = [], []
     for src in _sources():
         obj = os.path.join(OBJ, os.path.basename(src)[:-3] + ".o")
-        cmd = [NVCC, *ARCH, *FLAGS, "-c", src, "-o", obj]
-        if verbose:
-            print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
+        cmds.append([NVCC, *ARCH, *FLAGS, "-c", src, "-o", obj])
         objs.append(obj)
+    # the translation units are independent: compile them side by side
+    with concurrent.futures.ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as ex:
+        for cmd, _ in zip(cmds, ex.map(lambda c: subprocess.run(c, check=True), cmds)):
+            if verbose:
+                print(" ".join(cmd), flush=True)
     tmp = LIB + ".tmp"
     cmd = [NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lpthread"]
     if verbose:

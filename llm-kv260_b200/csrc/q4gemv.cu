@@ -32,7 +32,9 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 
+#include <atomic>
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -264,18 +266,24 @@ KernelFn pick_kernel(int layout, int xmode) {
 constexpr int kMaxDevices = 64;
 
 struct DeviceInfo {
+    std::atomic<int> ready{0};  // 1 once the fields below are written (release / acquire)
     int sms = 0;
     int smem_optin = 0;
     unsigned *status = nullptr;
 };
 
-// Per-device attributes, read once (launch paths are latency-critical).
+// Per-device attributes, read once (launch paths are latency-critical). The
+// first call on a device fills its entry under a lock; later calls read it
+// after an acquire load of `ready`, so a thread never sees a half-written entry.
 static DeviceInfo *device_info() {
     static DeviceInfo info[kMaxDevices];
+    static std::mutex fill_mu;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
     DeviceInfo &d = info[dev];
-    if (d.sms == 0) {
+    if (d.ready.load(std::memory_order_acquire)) return &d;
+    std::lock_guard<std::mutex> lock(fill_mu);
+    if (!d.ready.load(std::memory_order_relaxed)) {
         int sms = 0, smem = 0;
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return nullptr;
         if (cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return nullptr;
@@ -284,6 +292,7 @@ static DeviceInfo *device_info() {
         d.status = static_cast<unsigned *>(st);
         d.smem_optin = smem;
         d.sms = sms;
+        d.ready.store(1, std::memory_order_release);
     }
     return &d;
 }

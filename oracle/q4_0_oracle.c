@@ -12,6 +12,9 @@
 
 #include <math.h>
 #include <pthread.h>
+#include <sched.h>
+#include <stdatomic.h>
+#include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -21,9 +24,14 @@
 
 /* ------------------------------------------------------------ threads */
 
-/* Rows are independent, so a static split over POSIX threads gives the same
- * bits as one thread. (No OpenMP: the oracle shares a process with torch,
- * which brings its own OpenMP runtime.) */
+/* Rows are independent, so a static split over threads gives the same bits
+ * as one thread. (No OpenMP: the oracle shares a process with torch, which
+ * brings its own OpenMP runtime.) The workers persist between calls: a
+ * tensor-parallel decode simulates up to 8 ranks, so one token makes several
+ * hundred small GEMV calls, and a thread start per call would cost more than
+ * the rows themselves. Workers spin briefly on the job counter, then sleep on
+ * a condition variable. One caller at a time uses the pool; a second,
+ * concurrent caller starts its own threads for that call. */
 typedef struct {
     void (*fn)(void *ctx, int64_t lo, int64_t hi);
     void *ctx;
@@ -36,10 +44,7 @@ static void *span_run(void *arg) {
     return NULL;
 }
 
-static void parallel_rows(int64_t n, int threads, void (*fn)(void *, int64_t, int64_t), void *ctx) {
-    if (threads > 256) threads = 256;
-    if (threads < 2 || n < 2) { fn(ctx, 0, n); return; }
-    if (threads > n) threads = (int)n;
+static void spawn_rows(int64_t n, int threads, void (*fn)(void *, int64_t, int64_t), void *ctx) {
     pthread_t tid[256];
     span_t span[256];
     for (int t = 0; t < threads; ++t) {
@@ -56,6 +61,76 @@ static void parallel_rows(int64_t n, int threads, void (*fn)(void *, int64_t, in
     }
     fn(ctx, span[0].lo, span[0].hi);
     for (int t = 1; t < threads; ++t) if (span[t].fn) pthread_join(tid[t], NULL);
+}
+
+enum { POOL_MAX = 256 };
+static pthread_mutex_t pool_busy = PTHREAD_MUTEX_INITIALIZER;   /* held by the pool's one caller */
+static pthread_mutex_t pool_mu = PTHREAD_MUTEX_INITIALIZER;
+static pthread_cond_t pool_cv = PTHREAD_COND_INITIALIZER;
+static int pool_workers;                  /* started so far (never stopped) */
+static _Atomic unsigned pool_gen;         /* job number, bumped per call */
+static _Atomic int pool_left;             /* spans of the current job not yet done */
+static span_t pool_span[POOL_MAX];
+static int pool_nspans;
+static unsigned pool_gen0[POOL_MAX];      /* the job number when worker i started */
+
+static void *pool_worker(void *arg) {
+    const int id = (int)(intptr_t)arg; /* 1 .. */
+    unsigned seen = pool_gen0[id];
+    for (;;) {
+        unsigned g;
+        int spins = 0;
+        while ((g = atomic_load_explicit(&pool_gen, memory_order_acquire)) == seen) {
+            if (++spins < 20000) {
+                sched_yield();
+                continue;
+            }
+            pthread_mutex_lock(&pool_mu);
+            while ((g = atomic_load_explicit(&pool_gen, memory_order_acquire)) == seen) pthread_cond_wait(&pool_cv, &pool_mu);
+            pthread_mutex_unlock(&pool_mu);
+            break;
+        }
+        seen = g;
+        if (id < pool_nspans) {
+            const span_t *s = &pool_span[id];
+            s->fn(s->ctx, s->lo, s->hi);
+            atomic_fetch_sub_explicit(&pool_left, 1, memory_order_acq_rel);
+        }
+    }
+    return NULL;
+}
+
+static void parallel_rows(int64_t n, int threads, void (*fn)(void *, int64_t, int64_t), void *ctx) {
+    if (threads > POOL_MAX) threads = POOL_MAX;
+    if (threads < 2 || n < 2) { fn(ctx, 0, n); return; }
+    if (threads > n) threads = (int)n;
+    if (pthread_mutex_trylock(&pool_busy) != 0) {
+        spawn_rows(n, threads, fn, ctx);
+        return;
+    }
+    while (pool_workers < threads - 1) {
+        pthread_t tid;
+        pool_gen0[pool_workers + 1] = atomic_load(&pool_gen);
+        if (pthread_create(&tid, NULL, pool_worker, (void *)(intptr_t)(pool_workers + 1))) break;
+        pthread_detach(tid);
+        ++pool_workers;
+    }
+    if (threads > pool_workers + 1) threads = pool_workers + 1;
+    for (int t = 0; t < threads; ++t) {
+        pool_span[t].fn = fn;
+        pool_span[t].ctx = ctx;
+        pool_span[t].lo = n * t / threads;
+        pool_span[t].hi = n * (t + 1) / threads;
+    }
+    pool_nspans = threads;
+    atomic_store_explicit(&pool_left, threads - 1, memory_order_relaxed);
+    pthread_mutex_lock(&pool_mu);
+    atomic_fetch_add_explicit(&pool_gen, 1u, memory_order_release);
+    pthread_cond_broadcast(&pool_cv);
+    pthread_mutex_unlock(&pool_mu);
+    fn(ctx, pool_span[0].lo, pool_span[0].hi);
+    while (atomic_load_explicit(&pool_left, memory_order_acquire) > 0) sched_yield();
+    pthread_mutex_unlock(&pool_busy);
 }
 
 /* ------------------------------------------------------------ float16 */

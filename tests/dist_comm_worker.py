@@ -75,7 +75,7 @@ def main() -> None:
     comm.allgather(mine, allg, 16)
     eng.sync()
     res["allgather"] = allg.cpu().tolist() == [r * 10 + j for r in range(world) for j in range(4)]
-    vals = [1.5, 2.5, 2.5, 0.5][:world]                 # a tie between ranks 1 and 2: the lower index wins
+    vals = [1.5, 2.5, 2.5, 0.5, -1.0, 2.0, 0.25, 2.5][:world]   # ties at 2.5: the lowest rank's index wins
     sel = torch.tensor([rank * 1000 + 7], dtype=torch.int32)
     sel = torch.cat([sel, torch.tensor([vals[rank]], dtype=torch.float32).view(torch.int32)]).cuda()
     best = torch.zeros(2, dtype=torch.int32, device="cuda")

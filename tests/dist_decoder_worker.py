@@ -16,8 +16,11 @@ import torch.distributed as dist
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
 
-HD64 = dict(n_layer=2, n_embd=512, n_ff=1024, n_head=8, n_head_kv=2, head_dim=64, n_vocab=1024,
-            rope_base=500000.0, rms_eps=1e-5)
+# the 1B's attention geometry and width (8 KV heads, d_model 2048), so 2, 4 and
+# 8 ranks all divide it; two layers, a narrower FFN and vocabulary keep the
+# oracle quick
+TPW = dict(n_layer=2, n_embd=2048, n_ff=2048, n_head=32, n_head_kv=8, head_dim=64, n_vocab=2048,
+           rope_base=500000.0, rms_eps=1e-5)
 
 
 def bits(a) -> np.ndarray:
@@ -35,12 +38,12 @@ def main() -> None:
     from llm_kv260_b200 import model
     from llm_kv260_b200.comm import OrderedAllReduce
     from oracle import oracle
-    m = model.synth_model(HD64, seed=31)
-    prompt = model.random_prompt(5, HD64["n_vocab"], seed=32)
+    m = model.synth_model(TPW, seed=31)
+    prompt = model.random_prompt(5, TPW["n_vocab"], seed=32)
     res = {}
     for mode in ("graph", "persistent"):
         r = {"forward": True, "generate": True}
-        comm = OrderedAllReduce(rank, world, dev, HD64["n_embd"] + 256)
+        comm = OrderedAllReduce(rank, world, dev, TPW["n_embd"] + 256)
         dec = pkg.Decoder(m, device=dev, rank=rank, nranks=world, comm=comm, ctx_max=48,
                           persistent=mode == "persistent")
         ref = oracle.Decoder(m, nranks=world, ctx_max=48)

@@ -1,9 +1,9 @@
 """Generate tests/golden/golden.json by running the REFERENCE contract itself.
 
-    python tests/golden/gen_golden.py [/path/to/reference]
+    python tests/golden/gen_golden.py /path/to/reference
 
-Imports ``llm_kv260.q4_0`` from the reference checkout (default
-``$REFERENCE_SRC`` or the checkout this build was surveyed against) and records
+Imports ``llm_kv260.q4_0`` from the reference checkout named on the command
+line and records
 what it computes on the seeded inputs of ``cases.py``: the reference's own
 golden digest, the gen_vectors.py cases, the Q8_0 rounding edges, and every
 Llama-3.2-1B GEMV shape unsharded and K-split 2/4/8 ways with the rank-ordered
@@ -123,5 +123,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("REFERENCE_ROOT", "/root/reference")
-    main(root)
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/gen_golden.py <path of the llm-kv260 reference checkout>")
+    main(sys.argv[1])

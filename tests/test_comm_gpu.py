@@ -1,4 +1,4 @@
-"""The NVLink exchange on 2 GPUs (one process each), against the rank-ordered
+"""The NVLink exchange on 2, 4 and 8 GPUs (one process each), against the rank-ordered
 sum of board/tp/tp_llama.cpp:515-521: eager, graph-replayed, all-gather,
 greedy pick, and a peer that never comes (bounded wait, status set)."""
 
@@ -24,17 +24,18 @@ def _free_port() -> int:
     return port
 
 
-def test_exchange_on_two_gpus(cuda_lib, tmp_path):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_exchange_on_n_gpus(cuda_lib, tmp_path, world):
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs (one process per GPU); this box has fewer")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs (one process per GPU); this box has {torch.cuda.device_count()}")
     env = dict(os.environ, PYTHONPATH=ROOT + os.pathsep + os.environ.get("PYTHONPATH", ""))
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2", "--master-addr",
-           "127.0.0.1", "--master-port", str(_free_port()), os.path.join(ROOT, "tests", "dist_comm_worker.py"),
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), os.path.join(ROOT, "tests", "dist_comm_worker.py"),
            str(tmp_path)]
     proc = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
-    for r in range(2):
+    for r in range(world):
         with open(tmp_path / f"rank{r}.json") as fh:
             res = json.load(fh)
         assert res["eager"] and res["graph"] and res["allgather"] and res["pick"] and res["status_clean"], res

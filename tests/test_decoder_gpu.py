@@ -124,10 +124,43 @@ def test_decoder_argument_errors(cuda_lib, pkg):
         pd.step(17)                              # past ctx_max from position 0
 
 
+@pytest.fixture(scope="module")
+def config3_reference(oracle):
+    """BASELINE config 3 on the oracle: the random-init Llama-3.2-1B-shaped
+    model, a 24-token prompt, then 400 greedy tokens (positions up to 423)."""
+    from llm_kv260_b200 import model
+    m = model.synth_model(model.LLAMA_1B, seed=20260101)
+    prompt = model.random_prompt(24, model.LLAMA_1B["n_vocab"], seed=24)
+    ref = oracle.Decoder(m, nranks=1, ctx_max=424)
+    want = ref.generate(prompt, 401)
+    out = (m, prompt, want, ref.residual(), ref.logits())
+    ref.close()
+    return out
+
+
 @pytest.mark.gpu
-def test_tensor_parallel_decode_on_two_gpus(cuda_lib, tmp_path):
-    """Two ranks (one process per GPU) exchanging K-split partials inside the
-    o and down GEMVs: bit-exact to the oracle's two-rank simulation."""
+@MODES
+def test_config3_400_greedy_tokens(cuda_lib, pkg, config3_reference, persistent):
+    """The benchmarked workload itself: 401 tokens (the prompt's pick, then 400
+    forwards to position 423) identical to the oracle's, and the last
+    forward's residual stream and logits bit for bit."""
+    m, prompt, want, res, logits = config3_reference
+    dec = pkg.Decoder(m, ctx_max=424, persistent=persistent)
+    toks, _, _ = dec.generate(prompt, 401)
+    bad = np.nonzero(np.asarray(toks) != np.asarray(want))[0]
+    assert bad.size == 0, f"first differing token at generated index {bad[0]}"
+    assert np.array_equal(bits(dec.residual()), bits(res))
+    assert np.array_equal(bits(dec.logits()), bits(logits))
+    assert dec.status() == 0
+    dec.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tensor_parallel_decode_on_n_gpus(cuda_lib, tmp_path, world):
+    """2, 4 or 8 ranks (one process per GPU) exchanging K-split partials inside
+    the o and down GEMVs, on a model with the 1B's width (so 8 ranks divide
+    it): bit-exact to the oracle's simulation of the same ranks."""
     import json
     import os
     import socket
@@ -135,20 +168,20 @@ def test_tensor_parallel_decode_on_two_gpus(cuda_lib, tmp_path):
     import sys
 
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs (one process per GPU); this box has fewer")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs (one process per GPU); this box has {torch.cuda.device_count()}")
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
     env = dict(os.environ, PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2", "--master-addr",
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}", "--master-addr",
            "127.0.0.1", "--master-port", str(port), os.path.join(root, "tests", "dist_decoder_worker.py"),
            str(tmp_path)]
-    proc = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    proc = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
-    for r in range(2):
+    for r in range(world):
         with open(tmp_path / f"rank{r}.json") as fh:
             res = json.load(fh)
         for mode in ("graph", "persistent"):
