@@ -129,11 +129,18 @@ B200_API int b200_decoder_trace(b200_decoder_t *d, int tokens);
  * out (the outputs since are not valid). Reading clears it. */
 B200_API int b200_decoder_status(b200_decoder_t *d, unsigned *status);
 
-/* The RoPE table the decoder uploads (rope_table, tp_llama.cpp:574-580, no
- * frequency factors): cs[2i] = cosf(theta_i), cs[2i+1] = sinf(theta_i),
- * theta_i = pos * powf(base, -2i/d), computed on the host. No reference
+/* The model's RoPE frequency factors (rope_freqs.weight, head_dim/2 positive
+ * floats; tp_llama.cpp:282 loads them, 577-578 divides each angle by its
+ * factor), or NULL for none (the default). Recomputes the decoder's table. */
+B200_API int b200_decoder_set_rope_freqs(b200_decoder_t *d, const float *freqs);
+
+/* The RoPE table the decoder uploads (rope_table, tp_llama.cpp:574-580):
+ * cs[2i] = cosf(theta_i), cs[2i+1] = sinf(theta_i), theta_i = pos *
+ * powf(base, -2i/d), divided by freqs[i] when freqs is not NULL, computed on
+ * the host. b200_rope_table is the same without factors. No reference
  * counterpart as a function; exported so a caller can check the table. */
 B200_API int b200_rope_table(float *cs, int d, int pos, float base);
+B200_API int b200_rope_table_freqs(float *cs, int d, int pos, float base, const float *freqs);
 
 /* The decoder's CUDA stream (cudaStream_t). */
 B200_API void *b200_decoder_stream(b200_decoder_t *d);

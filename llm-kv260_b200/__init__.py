@@ -9,10 +9,11 @@ The directory name has a hyphen, so it is loaded by path as module
 
 from __future__ import annotations
 
-from . import capi, model
+from . import capi, gguf, model
 from .capi import B200Error, lib
 from .decoder import Decoder
+from .gguf import GGUFFile
 from .engine import LAYOUT_ROWS, LAYOUT_TILES, Engine, Gemv2Dev, GemvDev, QMat, Udmabuf, dev_ptr, tiled_bytes
 
-__all__ = ["B200Error", "Decoder", "Engine", "Gemv2Dev", "GemvDev", "LAYOUT_ROWS", "LAYOUT_TILES", "QMat", "Udmabuf", "capi",
-           "dev_ptr", "lib", "model", "tiled_bytes"]
+__all__ = ["B200Error", "Decoder", "Engine", "GGUFFile", "Gemv2Dev", "GemvDev", "LAYOUT_ROWS", "LAYOUT_TILES", "QMat",
+           "Udmabuf", "capi", "dev_ptr", "gguf", "lib", "model", "tiled_bytes"]

@@ -129,6 +129,14 @@ SIGNATURES: dict[str, tuple] = {
     "b200_decoder_status": (c_int, [c_vp, P(c_uint)]),
     "b200_decoder_trace": (c_int, [c_vp, c_int]),
     "b200_rope_table": (c_int, [c_vp, c_int, c_int, ctypes.c_float]),
+    "b200_rope_table_freqs": (c_int, [c_vp, c_int, c_int, ctypes.c_float, c_vp]),
+    "b200_decoder_set_rope_freqs": (c_int, [c_vp, c_vp]),
+    # b200_gguf.h
+    "b200_gguf_open": (c_int, [P(c_vp), c_char_p]),
+    "b200_gguf_close": (None, [c_vp]),
+    "b200_gguf_config": (c_int, [c_vp, P(b200_decoder_config_t)]),
+    "b200_gguf_tensor": (c_int, [c_vp, c_char_p, P(c_vp), P(c_u64), P(c_int), P(ctypes.c_int64)]),
+    "b200_decoder_load_gguf": (c_int, [c_vp, c_vp]),
     "b200_decoder_stream": (c_vp, [c_vp]),
     "b200_decoder_destroy": (c_int, [c_vp]),
     "b200_last_error": (c_char_p, []),

@@ -7,6 +7,7 @@
 #include <cstdint>
 
 #include "../../include/b200_comm.h"
+#include "../../include/b200_decoder.h"
 #include "q4gemv.h"
 
 namespace b200 {
@@ -29,6 +30,9 @@ struct AttnLaunch {
 };
 
 int attn_kv_stride(int ctx_max);  // ctx_max rounded up to a multiple of 8
+
+// The configuration a decoder was created with (decoder.cu; for the GGUF loader).
+int decoder_config(const b200_decoder_t *d, b200_decoder_config_t *out);
 int attn_smem_bytes(int head_dim, int kv_f16, int ctx_max);
 int attn_launch(const AttnLaunch &L, cudaStream_t stream);
 

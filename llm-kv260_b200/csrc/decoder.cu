@@ -842,15 +842,44 @@ extern "C" int b200_decoder_status(b200_decoder_t *d, unsigned *status) {
     return 0;
 }
 
-extern "C" int b200_rope_table(float *cs, int d, int pos, float base) {
+extern "C" int b200_rope_table_freqs(float *cs, int d, int pos, float base, const float *freqs) {
     if (!cs || d <= 0 || d % 2 || pos < 0) return dfail(kErrInval, "rope table: bad arguments");
     for (int i = 0; i < d / 2; ++i) {
-        const float theta = static_cast<float>(pos) * powf(base, -2.0f * static_cast<float>(i) / static_cast<float>(d));
+        float theta = static_cast<float>(pos) * powf(base, -2.0f * static_cast<float>(i) / static_cast<float>(d));
+        if (freqs) theta = theta / freqs[i];
         cs[2 * i] = cosf(theta);
         cs[2 * i + 1] = sinf(theta);
     }
     return 0;
 }
+
+extern "C" int b200_rope_table(float *cs, int d, int pos, float base) {
+    return b200_rope_table_freqs(cs, d, pos, base, nullptr);
+}
+
+extern "C" int b200_decoder_set_rope_freqs(b200_decoder_t *d, const float *freqs) {
+    if (!d) return dfail(kErrInval, "decoder: null handle");
+    if (freqs)
+        for (int i = 0; i < d->c.head_dim / 2; ++i)
+            if (!(freqs[i] > 0.0f)) return dfail(kErrInval, "decoder: rope_freqs[%d] is not a positive factor", i);
+    if (int rc = use_dev(d)) return rc;
+    const b200_decoder_config_t &c = d->c;
+    std::vector<float> cs(static_cast<size_t>(c.ctx_max) * c.head_dim);
+    for (int p = 0; p < c.ctx_max; ++p)
+        b200_rope_table_freqs(cs.data() + static_cast<size_t>(p) * c.head_dim, c.head_dim, p, c.rope_base, freqs);
+    if (cudaStreamSynchronize(d->stream) != cudaSuccess) return dfail(kErrCuda, "decoder: stream failed");
+    if (cudaMemcpy(d->rope_cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        return dfail(kErrCuda, "decoder: rope table upload failed");
+    return 0;
+}
+
+namespace b200 {
+int decoder_config(const b200_decoder_t *d, b200_decoder_config_t *out) {
+    if (!d || !out) return dfail(kErrInval, "decoder: null argument");
+    *out = d->c;
+    return 0;
+}
+}  // namespace b200
 
 extern "C" void *b200_decoder_stream(b200_decoder_t *d) { return d ? d->stream : nullptr; }
 

@@ -19,19 +19,22 @@ class Decoder:
     """One rank's decoder. `model` is a dict as model.synth_model returns (or a
     GGUF loader would): hparams, "layers", "token_embd", "output_norm"."""
 
-    def __init__(self, model: dict, device: int = 0, rank: int = 0, nranks: int = 1, comm=None,
+    def __init__(self, model: dict | None, device: int = 0, rank: int = 0, nranks: int = 1, comm=None,
                  ctx_max: int = 512, kv_f16: bool = True, round_mode: int = 0, exact_norm: bool = False,
-                 persistent: bool = False):
-        c = capi.b200_decoder_config_t()
-        for n in ("n_layer", "n_embd", "n_ff", "n_head", "n_head_kv", "head_dim", "n_vocab"):
-            setattr(c, n, int(model[n]))
-        c.rope_base, c.rms_eps = float(model["rope_base"]), float(model["rms_eps"])
+                 persistent: bool = False, _cfg=None):
+        c = _cfg if _cfg is not None else capi.b200_decoder_config_t()
+        if model is not None:
+            for n in ("n_layer", "n_embd", "n_ff", "n_head", "n_head_kv", "head_dim", "n_vocab"):
+                setattr(c, n, int(model[n]))
+            c.rope_base, c.rms_eps = float(model["rope_base"]), float(model["rms_eps"])
         c.ctx_max, c.kv_f16, c.round_mode, c.exact_norm = ctx_max, int(kv_f16), round_mode, int(exact_norm)
         c.persistent = int(persistent)
         self.cfg, self.rank, self.nranks, self.ctx_max = c, rank, nranks, ctx_max
         self.h = ctypes.c_void_p()
         check(lib().b200_decoder_create(ctypes.byref(self.h), ctypes.byref(c), device, rank, nranks,
                                         comm.h if comm is not None else None), "b200_decoder_create")
+        if model is None:
+            return
         for i, L in enumerate(model["layers"]):
             arrs = [np.ascontiguousarray(L[n]) for n in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate",
                                                         "ffn_up", "ffn_down")]
@@ -41,6 +44,34 @@ class Decoder:
         te = np.ascontiguousarray(model["token_embd"])
         on = np.ascontiguousarray(model["output_norm"], dtype=np.float32)
         check(lib().b200_decoder_set_output(self.h, _p(te), _p(on)), "b200_decoder_set_output")
+        if model.get("rope_freqs") is not None:
+            self.set_rope_freqs(model["rope_freqs"])
+
+    @classmethod
+    def from_gguf(cls, path: str, **kw) -> "Decoder":
+        """A decoder for a GGUF Q4_0 model file (load_model, tp_llama.cpp:226-283):
+        hyperparameters from its llama.* keys, every tensor loaded (and this
+        rank's shard cut) through b200_decoder_load_gguf. Keyword arguments as
+        for the constructor (device, rank, nranks, comm, ctx_max, ...)."""
+        from .gguf import GGUFFile
+        with GGUFFile(path) as g:
+            dec = cls(None, _cfg=g.config(), **kw)
+            try:
+                check(lib().b200_decoder_load_gguf(dec.h, g.h), "b200_decoder_load_gguf")
+            except Exception:
+                dec.close()
+                raise
+        return dec
+
+    def set_rope_freqs(self, freqs) -> None:
+        """The model's rope_freqs factors (head_dim/2 floats), or None."""
+        if freqs is None:
+            check(lib().b200_decoder_set_rope_freqs(self.h, None), "b200_decoder_set_rope_freqs")
+            return
+        f = np.ascontiguousarray(freqs, dtype=np.float32)
+        if f.shape != (self.cfg.head_dim // 2,):
+            raise ValueError(f"rope_freqs must hold head_dim/2 = {self.cfg.head_dim // 2} factors")
+        check(lib().b200_decoder_set_rope_freqs(self.h, _p(f)), "b200_decoder_set_rope_freqs")
 
     def forward(self, token: int, pos: int) -> tuple[int, float]:
         """runtime::forward + the greedy pick over all ranks."""
@@ -119,8 +150,12 @@ class Decoder:
             pass
 
 
-def rope_table(d: int, pos: int, base: float) -> np.ndarray:
-    """The host RoPE table the decoder uploads (b200_rope_table)."""
+def rope_table(d: int, pos: int, base: float, freqs=None) -> np.ndarray:
+    """The host RoPE table the decoder uploads (b200_rope_table[_freqs])."""
     cs = np.empty(d, dtype=np.float32)
-    check(lib().b200_rope_table(_p(cs), d, pos, base), "b200_rope_table")
+    if freqs is None:
+        check(lib().b200_rope_table(_p(cs), d, pos, base), "b200_rope_table")
+    else:
+        f = np.ascontiguousarray(freqs, dtype=np.float32)
+        check(lib().b200_rope_table_freqs(_p(cs), d, pos, base, _p(f)), "b200_rope_table_freqs")
     return cs

@@ -64,15 +64,19 @@ void odec_rmsnorm(float *out, const float *x, const float *w, int n, float eps) 
     for (int i = 0; i < n; ++i) out[i] = (x[i] * scale) * w[i];
 }
 
-/* rope_table, tp_llama.cpp:574-580, without rope_freqs (random-init models
- * have none): theta_i = pos * base^(-2i/d), all in float. */
-void odec_rope_table(float *cs, int d, int pos, float base) {
+/* rope_table, tp_llama.cpp:574-580: theta_i = pos * base^(-2i/d), divided
+ * by the model's frequency factor freqs[i] when it has rope_freqs (Llama 3
+ * GGUFs do; random-init models do not), all in float. */
+void odec_rope_table_freqs(float *cs, int d, int pos, float base, const float *freqs) {
     for (int i = 0; i < d / 2; ++i) {
-        const float theta = (float)pos * powf(base, -2.0f * (float)i / (float)d);
+        float theta = (float)pos * powf(base, -2.0f * (float)i / (float)d);
+        if (freqs) theta = theta / freqs[i];
         cs[2 * i] = cosf(theta);
         cs[2 * i + 1] = sinf(theta);
     }
 }
+
+void odec_rope_table(float *cs, int d, int pos, float base) { odec_rope_table_freqs(cs, d, pos, base, NULL); }
 
 /* rope, tp_llama.cpp:581-591: adjacent pairs of every head. */
 void odec_rope(float *x, int n_heads, int d, const float *cs) {
@@ -181,7 +185,7 @@ typedef struct {
 struct odec {
     odec_config_t c;
     int q_rows, kv_rows, ff_rows, vocab_rows, o_k, down_k;
-    float **attn_norm, **ffn_norm, *output_norm;
+    float **attn_norm, **ffn_norm, *output_norm, *rope_freqs;
     uint8_t *token_embd;
     rank_t *rank;
     float *x, *h, *cs, *sum;
@@ -237,6 +241,7 @@ void odec_destroy(odec_t *d) {
     free(d->attn_norm);
     free(d->ffn_norm);
     free(d->output_norm);
+    free(d->rope_freqs);
     free(d->token_embd);
     free(d->rank);
     free(d->x);
@@ -308,7 +313,7 @@ int odec_create(odec_t **out, const odec_config_t *cfg, const odec_layer_t *laye
         R->gu_y = calloc((size_t)(2 * d->ff_rows), 4);
         R->act = calloc((size_t)d->ff_rows, 4);
         R->logits = calloc((size_t)d->vocab_rows, 4);
-        R->scores = calloc((size_t)4 * c.ctx_max, 4);
+        R->scores = calloc((size_t)4 * c.ctx_max * (c.n_head_kv / n), 4);   /* one score block per KV head */
         if (!R->layers || !R->lm_head || !R->kcache || !R->vcache || !R->qkv_y || !R->attn || !R->partial ||
             !R->gu_y || !R->act || !R->logits || !R->scores) {
             odec_destroy(d);
@@ -400,15 +405,53 @@ static void pick(const odec_t *d, int *tok, float *val) {
     *val = av[best];
 }
 
+/* attention of (rank, KV head) items [lo, hi) of one layer at one position:
+ * the query heads of each KV head in groups of up to 4 (tp_llama.cpp:849-856) */
+typedef struct {
+    odec_t *d;
+    int l, pos;
+    float scale;
+} attn_job_t;
+
+static void attention_span(void *ctx, int64_t lo, int64_t hi) {
+    const attn_job_t *J = (const attn_job_t *)ctx;
+    const odec_t *d = J->d;
+    const odec_config_t *c = &d->c;
+    const int hd = c->head_dim, kvh_local = c->n_head_kv / c->nranks, group = c->n_head / c->n_head_kv;
+    const int esz = c->kv_f16 ? 2 : 4;
+    for (int64_t it = lo; it < hi; ++it) {
+        const int r = (int)(it / kvh_local), kvh = (int)(it % kvh_local);
+        const rank_t *R = &d->rank[r];
+        const float *q = R->qkv_y;
+        const int64_t base = ((int64_t)J->l * kvh_local + kvh) * c->ctx_max * hd;
+        const void *kc0 = (const uint8_t *)R->kcache + base * esz;
+        const void *vc0 = (const uint8_t *)R->vcache + base * esz;
+        float *sc = R->scores + (int64_t)kvh * 4 * c->ctx_max;
+        for (int g0 = 0; g0 < group; g0 += 4) {
+            const int hq = kvh * group + g0;
+            const int B = group - g0 < 4 ? group - g0 : 4;
+            odec_attention(B, q + hq * hd, kc0, vc0, c->kv_f16, hd, J->pos, hd, J->scale, sc, c->ctx_max,
+                           R->attn + hq * hd);
+        }
+    }
+}
+
+int odec_set_rope_freqs(odec_t *d, const float *freqs) {
+    if (!d) return -2;
+    free(d->rope_freqs);
+    d->rope_freqs = freqs ? copy_f32(freqs, d->c.head_dim / 2) : NULL;
+    return freqs && !d->rope_freqs ? -2 : 0;
+}
+
 int odec_forward(odec_t *d, int token, int pos, int *tok, float *val) {
     if (!d || !tok || !val) return -2;
     const odec_config_t *c = &d->c;
     if (token < 0 || token >= c->n_vocab || pos < 0 || pos >= c->ctx_max) return -2;
     const int n = c->nranks, e = c->n_embd, hd = c->head_dim;
-    const int heads_local = c->n_head / n, kvh_local = c->n_head_kv / n, group = c->n_head / c->n_head_kv;
+    const int heads_local = c->n_head / n, kvh_local = c->n_head_kv / n;
     const float scale = 1.0f / sqrtf((float)hd);
     odec_embed(d->x, d->token_embd, token, e);
-    odec_rope_table(d->cs, hd, pos, c->rope_base);
+    odec_rope_table_freqs(d->cs, hd, pos, c->rope_base, d->rope_freqs);
     for (int l = 0; l < c->n_layer; ++l) {
         odec_rmsnorm(d->h, d->x, d->attn_norm[l], e, c->rms_eps);
         for (int r = 0; r < n; ++r) {
@@ -430,20 +473,12 @@ int odec_forward(odec_t *d, int token, int pos, int *tok, float *val) {
                     }
                 }
             }
-            const int esz = c->kv_f16 ? 2 : 4;
-            for (int kvh = 0; kvh < kvh_local; ++kvh) {
-                const int64_t base = ((int64_t)l * kvh_local + kvh) * c->ctx_max * hd;
-                const void *kc0 = (const uint8_t *)R->kcache + base * esz;
-                const void *vc0 = (const uint8_t *)R->vcache + base * esz;
-                for (int g0 = 0; g0 < group; g0 += 4) {
-                    const int hq = kvh * group + g0;
-                    const int B = group - g0 < 4 ? group - g0 : 4;
-                    odec_attention(B, q + hq * hd, kc0, vc0, c->kv_f16, hd, pos, hd, scale, R->scores, c->ctx_max,
-                                   R->attn + hq * hd);
-                }
-            }
-            gemv(d, L->o, e, d->o_k, R->attn, R->partial);
         }
+        /* the KV heads are independent (each has its own score rows): run
+         * them side by side, each in the reference's order */
+        attn_job_t job = {d, l, pos, scale};
+        oracle_parallel_for((int64_t)n * kvh_local, c->threads, attention_span, &job);
+        for (int r = 0; r < n; ++r) gemv(d, d->rank[r].layers[l].o, e, d->o_k, d->rank[r].attn, d->rank[r].partial);
         allreduce_add(d);
         odec_rmsnorm(d->h, d->x, d->ffn_norm[l], e, c->rms_eps);
         for (int r = 0; r < n; ++r) {

@@ -66,6 +66,10 @@ void odec_destroy(odec_t *d);
  * pick over all ranks: *pick = the token, *value = its logit. */
 int odec_forward(odec_t *d, int token, int pos, int *pick, float *value);
 
+/* The model's rope_freqs factors (head_dim/2 floats, tp_llama.cpp:577-578,
+ * 282), or NULL for none (the default). */
+int odec_set_rope_freqs(odec_t *d, const float *freqs);
+
 /* runtime::generate (tp_llama.cpp:942-968) with temperature 0 and no EOG:
  * the prompt at positions 0..n_prompt-1, then n_gen tokens into out
  * (n_prompt + n_gen - 1 forward calls). */
@@ -79,6 +83,7 @@ int odec_read(odec_t *d, int what, int rank, float *out, int64_t n);
 float odec_v_expf(float x);                                              /* tp_llama.cpp:530-553 */
 void odec_rmsnorm(float *out, const float *x, const float *w, int n, float eps);   /* 557-569 */
 void odec_rope_table(float *cs, int d, int pos, float base);            /* 574-580, no freq factors */
+void odec_rope_table_freqs(float *cs, int d, int pos, float base, const float *freqs);   /* 574-580 */
 void odec_rope(float *x, int n_heads, int d, const float *cs);          /* 581-591 */
 void odec_silu_mul(float *act, const float *gate, const float *up, int n);   /* 615-622 */
 void odec_embed(float *out, const uint8_t *token_embd, int token, int n_embd);   /* 593-604 */

@@ -66,6 +66,8 @@ def lib() -> ctypes.CDLL:
             "odec_v_expf": (ctypes.c_float, [ctypes.c_float]),
             "odec_rmsnorm": (None, [P, P, P, I, ctypes.c_float]),
             "odec_rope_table": (None, [P, I, I, ctypes.c_float]),
+            "odec_rope_table_freqs": (None, [P, I, I, ctypes.c_float, P]),
+            "odec_set_rope_freqs": (I, [P, P]),
             "odec_rope": (None, [P, I, I, P]),
             "odec_silu_mul": (None, [P, P, P, I]),
             "odec_embed": (None, [P, P, I, I]),
@@ -274,6 +276,14 @@ def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
     return out
 
 
+def rope_table_freqs(d: int, pos: int, base: float, freqs: np.ndarray) -> np.ndarray:
+    """tp_llama.cpp:574-580 with the model's frequency factors."""
+    cs = np.empty(d, dtype=np.float32)
+    f = np.ascontiguousarray(freqs, dtype=np.float32)
+    lib().odec_rope_table_freqs(_ptr(cs), d, pos, base, _ptr(f))
+    return cs
+
+
 def rope_table(d: int, pos: int, base: float) -> np.ndarray:
     """tp_llama.cpp:574-580 without freq factors: cos, sin interleaved, d floats."""
     cs = np.empty(d, dtype=np.float32)
@@ -362,6 +372,11 @@ class Decoder:
         self._h = ctypes.c_void_p()
         _check(lib().odec_create(ctypes.byref(self._h), ctypes.byref(c), ctypes.cast(layers, ctypes.c_void_p),
                                  _ptr(te), _ptr(on)), "odec_create")
+        if model.get("rope_freqs") is not None:
+            rf = np.ascontiguousarray(model["rope_freqs"], dtype=np.float32)
+            if rf.shape != (c.head_dim // 2,):
+                raise ValueError(f"rope_freqs must hold head_dim/2 = {c.head_dim // 2} factors")
+            _check(lib().odec_set_rope_freqs(self._h, _ptr(rf)), "odec_set_rope_freqs")
 
     def forward(self, token: int, pos: int) -> tuple[int, float]:
         t, v = ctypes.c_int(0), ctypes.c_float(0.0)
@@ -388,6 +403,108 @@ class Decoder:
     def close(self) -> None:
         if self._h:
             lib().odec_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------- the reference's own runtime
+# oracle/_ref/libref_runtime.so: board/tp/tp_llama.cpp's decode sections built
+# on this host (ref_runtime.cpp, refshim/). It exists only where the reference
+# checkout was present at build time; the golden fixtures it produced
+# (tests/golden/ref_decode.json) carry its results everywhere else.
+
+_REF_PATH = os.path.join(_HERE, "_ref", "libref_runtime.so")
+_ref = None
+
+
+def default_reference_root() -> str:
+    """Where build() looks for the reference checkout: $LLM_KV260_REFERENCE,
+    else a directory named "reference" beside this repository."""
+    return os.environ.get("LLM_KV260_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(_HERE)), "reference")
+
+
+def build_ref(reference_root: str, force: bool = False) -> str | None:
+    """Build oracle/_ref from the reference checkout at `reference_root`
+    (returns the library path), or None when the checkout is absent."""
+    tp = os.path.join(reference_root, "board", "tp", "tp_llama.cpp")
+    if not os.path.exists(tp):
+        return None
+    deps = [os.path.join(_HERE, f) for f in ("ref_runtime.cpp", "q4_0_oracle.c", "q4_0_oracle.h", "Makefile")]
+    deps += [os.path.join(_HERE, "refshim", f) for f in os.listdir(os.path.join(_HERE, "refshim"))] + [tp]
+    if force or not os.path.exists(_REF_PATH) or os.path.getmtime(_REF_PATH) < max(os.path.getmtime(f) for f in deps):
+        subprocess.run(["make", "-s", "-C", _HERE, "ref", f"REF={os.path.abspath(reference_root)}"], check=True)
+    return _REF_PATH
+
+
+def ref_available() -> bool:
+    return os.path.exists(_REF_PATH)
+
+
+def ref_lib() -> ctypes.CDLL:
+    global _ref
+    if _ref is None:
+        if not os.path.exists(_REF_PATH):
+            raise RuntimeError("oracle/_ref is not built (it needs the reference checkout)")
+        L = ctypes.CDLL(_REF_PATH)
+        P, I, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+        sig = {
+            "ref_open": (I, [ctypes.c_char_p, I, I, I, I, ctypes.POINTER(P)]),
+            "ref_forward": (I, [P, I, I, ctypes.POINTER(I), ctypes.POINTER(F)]),
+            "ref_read": (I, [P, I, I, P, ctypes.c_int64]),
+            "ref_close": (None, [P]),
+            "ref_v_expf4": (None, [P, P]),
+            "ref_rmsnorm": (None, [P, P, P, I, F]),
+            "ref_rope_table": (None, [P, I, I, F]),
+            "ref_rope": (None, [P, I, I, P]),
+            "ref_embed": (None, [P, P, I, I]),
+            "ref_silu_mul": (None, [P, P, P, I]),
+            "ref_softmax_exp": (F, [P, I, F]),
+            "ref_attention_heads": (None, [I, P, P, P, ctypes.c_int64, I, I, F, P, I, P]),
+            "ref_quantize_x": (None, [P, P, P, I]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = res, args
+        _ref = L
+    return _ref
+
+
+class RefRuntime:
+    """The reference runtime itself (runtime::init/forward/sample_token and
+    load_model, tp_llama.cpp), `nranks` ranks as threads, reading a GGUF file.
+    The engine is the FPGA's stand-in (the pinned q4_0 GEMV); float32 KV
+    cache and the runtime's roundf quantiser, as on the boards."""
+
+    def __init__(self, gguf_path: str, nranks: int = 1, ctx_max: int = 64, gemv2: bool = False,
+                 threads: int | None = None):
+        self._h = ctypes.c_void_p()
+        t = threads or max(1, default_threads() // nranks)
+        rc = ref_lib().ref_open(gguf_path.encode(), nranks, ctx_max, int(gemv2), t, ctypes.byref(self._h))
+        if rc:
+            raise RuntimeError(f"the reference runtime refused the model (rc {rc})")
+        self.nranks = nranks
+
+    def forward(self, token: int, pos: int) -> tuple[int, float]:
+        t, v = ctypes.c_int(0), ctypes.c_float(0.0)
+        rc = ref_lib().ref_forward(self._h, token, pos, ctypes.byref(t), ctypes.byref(v))
+        if rc:
+            raise RuntimeError(f"ref_forward failed ({rc})")
+        return int(t.value), float(v.value)
+
+    def read(self, what: int, n: int, rank: int = 0) -> np.ndarray:
+        out = np.empty(n, dtype=np.float32)
+        if ref_lib().ref_read(self._h, what, rank, _ptr(out), n):
+            raise RuntimeError("ref_read refused the size")
+        return out
+
+    def close(self) -> None:
+        if self._h:
+            ref_lib().ref_close(self._h)
             self._h = ctypes.c_void_p()
 
     def __del__(self):

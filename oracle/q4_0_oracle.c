@@ -133,6 +133,10 @@ static void parallel_rows(int64_t n, int threads, void (*fn)(void *, int64_t, in
     pthread_mutex_unlock(&pool_busy);
 }
 
+void oracle_parallel_for(int64_t n, int threads, void (*fn)(void *, int64_t, int64_t), void *ctx) {
+    parallel_rows(n, threads, fn, ctx);
+}
+
 /* ------------------------------------------------------------ float16 */
 
 uint16_t oracle_f32_to_f16(float f) {

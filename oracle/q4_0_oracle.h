@@ -81,6 +81,10 @@ int64_t oracle_gemv2_chunk_offset(int r, int c, int rows, int k, int *port);
  * tp_llama.cpp:515-521): s = p0; s = s + p_r for r = 1..n-1, per element. */
 int oracle_allreduce_ordered(const float *const *partials, int n, int64_t len, float *out);
 
+/* Run fn(ctx, lo, hi) over [0, n) split across `threads` threads (the
+ * oracle's worker pool); for independent items only. */
+void oracle_parallel_for(int64_t n, int threads, void (*fn)(void *ctx, int64_t lo, int64_t hi), void *ctx);
+
 #ifdef __cplusplus
 }
 #endif

@@ -69,6 +69,37 @@ def main() -> None:
         dec.close()
         comm.close()
         res[mode] = r
+    # the reference runtime's own results for this many ranks
+    # (tests/golden/ref_decode.json), each model loaded from a GGUF file
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import cases
+    from gguf_model import write_gguf
+    from test_decoder_gpu import check_reference_fixture
+    with open(os.path.join(ROOT, "tests", "golden", "ref_decode.json")) as fh:
+        fixtures = json.load(fh)["cases"]
+    res["reference"] = {}
+    for name, spec in sorted(cases.REF_DECODE_CASES.items()):
+        if spec[2] != world:
+            continue
+        path = os.path.join(out_dir, f"{name}.gguf")
+        if rank == 0:
+            m, _ = cases.ref_decode_model(name)
+            write_gguf(m, path, rope_freqs=m.get("rope_freqs"))
+        dist.barrier()
+        for mode in ("graph", "persistent"):
+            comm = OrderedAllReduce(rank, world, dev, spec[0]["n_embd"] + 256)
+            dec = pkg.Decoder.from_gguf(path, device=dev, rank=rank, nranks=world, comm=comm, ctx_max=spec[4],
+                                        kv_f16=False, round_mode=1, persistent=mode == "persistent")
+            try:
+                check_reference_fixture(dec, name, fixtures[name], rank)
+                ok = dec.status() == 0
+            except AssertionError as e:
+                ok = str(e)
+            dist.barrier()
+            dec.close()
+            comm.close()
+            res["reference"][f"{name}/{mode}"] = ok
     with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as fh:
         json.dump(res, fh)
     dist.destroy_process_group()

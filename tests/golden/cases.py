@@ -97,3 +97,61 @@ def q8_edge_inputs() -> dict[str, np.ndarray]:
     tiny = np.full(32, 1e-30, dtype=np.float32)
     tiny[::3] = -1e-30
     return {"roundf_tie": tie, "floor_half": half, "zero": zero, "negzero": negzero, "tiny": tiny}
+
+
+# ------------------------------------------------------------------ decode
+# Random-init models run through the reference runtime's own decode code
+# (oracle/_ref: tp_llama.cpp's load_model, forward and sample_token compiled
+# on the host, float32 KV cache, the runtime's roundf quantiser) by
+# gen_ref_decode.py; ref_decode.json holds, per case, the greedy token and
+# the SHA-256 of the residual stream after every forward, and every rank's
+# logits digest at the last one.
+
+HD64 = dict(n_layer=2, n_embd=512, n_ff=1024, n_head=8, n_head_kv=2, head_dim=64, n_vocab=1024,
+            rope_base=500000.0, rms_eps=1e-5)
+HD128_G3 = dict(n_layer=2, n_embd=1536, n_ff=1536, n_head=12, n_head_kv=4, head_dim=128, n_vocab=1024,
+                rope_base=500000.0, rms_eps=1e-5)
+HD64_1L = dict(HD64, n_layer=1)
+TPW = dict(n_layer=2, n_embd=2048, n_ff=8192, n_head=32, n_head_kv=8, head_dim=64, n_vocab=2048,
+           rope_base=500000.0, rms_eps=1e-5)
+W3B = dict(n_layer=1, n_embd=3072, n_ff=8192, n_head=24, n_head_kv=8, head_dim=128, n_vocab=2048,
+           rope_base=500000.0, rms_eps=1e-5)
+
+# name: (hparams, weight seed, ranks, prompt length, positions, gemv2 engine layout, rope_freqs).
+# The runtime sizes the engine's output buffer as max(vocab_rows, 2 * ff_rows)
+# floats (tp_llama.cpp:1277) and writes n_embd rows into it from the o and down
+# GEMVs, so every case keeps 2 * n_ff / ranks >= n_embd.
+REF_DECODE_CASES = {
+    "hd64_r1": (HD64, 41, 1, 6, 40, False, False),
+    "hd64_r2_gemv2": (HD64, 41, 2, 6, 40, True, False),
+    "hd128_g3_r1_freqs": (HD128_G3, 42, 1, 5, 24, False, True),
+    "hd128_g3_r2_freqs": (HD128_G3, 42, 2, 5, 24, True, True),
+    "long_r1": (HD64_1L, 43, 1, 290, 300, False, False),
+    "tpw_r4": (TPW, 44, 4, 5, 20, False, False),
+    "tpw_r8": (TPW, 44, 8, 5, 20, True, False),
+    "w3b_r1": (W3B, 45, 1, 5, 20, False, False),
+    "w3b_r4": (W3B, 45, 4, 5, 20, True, False),
+}
+
+
+def rope_freqs(head_dim: int) -> np.ndarray:
+    """Llama-3-style frequency factors: 1 for the high frequencies, rising
+    smoothly to 8 for the low ones (head_dim/2 float32)."""
+    t = np.linspace(0.0, 1.0, head_dim // 2, dtype=np.float64)
+    return (1.0 + 7.0 * np.clip((t - 0.3) / 0.5, 0.0, 1.0) ** 2).astype(np.float32)
+
+
+def ref_decode_model(name: str):
+    """(model dict, prompt) of a REF_DECODE_CASES entry."""
+    import importlib.util
+    import os
+    hp, seed, _, n_prompt, _, _, freqs = REF_DECODE_CASES[name]
+    here = os.path.dirname(os.path.abspath(__file__))
+    spec = importlib.util.spec_from_file_location("b200_case_model", os.path.join(here, "..", "..", "llm-kv260_b200",
+                                                                                  "model.py"))
+    mdl = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mdl)
+    m = mdl.synth_model(hp, seed=seed)
+    if freqs:
+        m["rope_freqs"] = rope_freqs(hp["head_dim"])
+    return m, mdl.random_prompt(n_prompt, hp["n_vocab"], seed=seed + 1000)

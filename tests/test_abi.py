@@ -11,7 +11,7 @@ import re
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADERS = ["gemv_dev.h", "gemv2_dev.h", "udmabuf.h", "b200_engine.h", "b200_comm.h", "b200_decoder.h"]
+HEADERS = ["gemv_dev.h", "gemv2_dev.h", "udmabuf.h", "b200_engine.h", "b200_comm.h", "b200_decoder.h", "b200_gguf.h"]
 
 
 def declared_symbols() -> set[str]:

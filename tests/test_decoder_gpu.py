@@ -41,6 +41,56 @@ def step_by_step(pkg, oracle, hp, seed, n_prompt, n_steps, ctx_max=64, **kw):
 MODES = pytest.mark.parametrize("persistent", [False, True], ids=["graph", "persistent"])
 
 
+def check_reference_fixture(dec, name: str, fixture: dict, rank: int = 0) -> None:
+    """Position by position, the decoder's greedy token, its logit and the
+    residual stream's digest against what the reference runtime's own code
+    computed (tests/golden/ref_decode.json), then this rank's last logits."""
+    import cases
+    _, _, _, n_prompt, n_pos, _, _ = cases.REF_DECODE_CASES[name]
+    prompt = fixture["prompt"]
+    tok = None
+    for i in range(n_pos):
+        inp = prompt[i] if i < n_prompt else tok
+        tok, val = dec.forward(inp, i)
+        assert tok == fixture["tokens"][i], f"{name}: token at position {i}"
+        assert int(np.float32(val).view(np.uint32)) == fixture["value_bits"][i], f"{name}: logit at position {i}"
+        assert cases.sha256(dec.residual()) == fixture["residual_sha256"][i], f"{name}: residual at position {i}"
+    assert cases.sha256(dec.logits()) == fixture["last_logits_sha256"][rank], f"{name}: logits"
+
+
+@pytest.fixture(scope="module")
+def ref_decode():
+    import json
+    import os
+    import cases
+    with open(os.path.join(os.path.dirname(cases.__file__), "ref_decode.json")) as fh:
+        return json.load(fh)["cases"]
+
+
+def _ref_cases(ranks: int) -> list[str]:
+    import cases
+    return sorted(n for n, c in cases.REF_DECODE_CASES.items() if c[2] == ranks)
+
+
+@pytest.mark.gpu
+@MODES
+@pytest.mark.parametrize("name", _ref_cases(1))
+def test_matches_reference_runtime_from_gguf(cuda_lib, pkg, ref_decode, tmp_path, persistent, name):
+    """The model as a GGUF file through the library's loader
+    (b200_decoder_load_gguf), float32 KV cache and the runtime's roundf
+    quantiser as on the boards: every token, logit and residual equal to the
+    reference runtime's (its own forward/sample_token compiled on the host)."""
+    import cases
+    from gguf_model import write_gguf
+    m, _ = cases.ref_decode_model(name)
+    path = write_gguf(m, str(tmp_path / f"{name}.gguf"), rope_freqs=m.get("rope_freqs"))
+    n_pos = cases.REF_DECODE_CASES[name][4]
+    dec = pkg.Decoder.from_gguf(path, ctx_max=n_pos, kv_f16=False, round_mode=1, persistent=persistent)
+    check_reference_fixture(dec, name, ref_decode[name])
+    assert dec.status() == 0
+    dec.close()
+
+
 @pytest.mark.gpu
 @MODES
 @pytest.mark.parametrize("kw", [dict(), dict(kv_f16=False), dict(round_mode=1), dict(exact_norm=True)],
@@ -186,3 +236,4 @@ def test_tensor_parallel_decode_on_n_gpus(cuda_lib, tmp_path, world):
             res = json.load(fh)
         for mode in ("graph", "persistent"):
             assert res[mode]["forward"] and res[mode]["generate"] and res[mode]["status"] == 0, (mode, res)
+        assert res["reference"] and all(v is True for v in res["reference"].values()), res["reference"]
