@@ -327,7 +327,56 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
     }
 }
 
+// Long contexts, where a cluster CTA's share of the head's K rows and V^T
+// columns no longer fits shared memory: one CTA per local KV head running
+// attn_core (attn_core.cuh), which streams K in 16 KB chunks and V^T in
+// 256-byte column chunks through double-buffered stages -- the same
+// operations in the same order (tp_llama.cpp:644-690), so the same bits.
+constexpr int kLongThreads = 256;
+constexpr int kLongColBytes = 256;
+__host__ __device__ constexpr int long_kc(int d, int esz) { return 16384 / (d * esz); }
+
+__host__ __device__ inline int attn_long_smem(int d, int esz, int stride) {
+    return attn_core_smem_bytes(d, esz, kLongColBytes, long_kc(d, esz), kLongThreads, stride);
+}
+
+template <int D, int ESZ>
+__global__ void __launch_bounds__(kLongThreads, 1) attn_long_kernel(const __grid_constant__ AttnParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t bars[kAttnBars];
+    const int kvh = blockIdx.x;
+    uint64_t *rec = attn_rec(p.trace);
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < kAttnBars; ++b) mbar_init(&bars[b], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+    attn_stamp_at(rec, 0);
+    pdl_wait_prior_grid();
+    attn_stamp_at(rec, 1);
+    const int n = *p.pos + 1;
+    const size_t head_bytes = static_cast<size_t>(p.stride) * D * ESZ;
+    uint32_t par = 0;
+    if (!attn_core<D, ESZ, kLongColBytes, long_kc(D, ESZ), kLongThreads>(
+            p.q + static_cast<size_t>(kvh) * p.group * D, p.kcache + kvh * head_bytes, p.vcache + kvh * head_bytes,
+            p.stride, n, p.group, p.scale, p.out + static_cast<size_t>(kvh) * p.group * D, smem, 1, bars, par, p.status,
+            rec) &&
+        threadIdx.x == 0)
+        atomicOr(p.status, kStatusStageTimeout);
+    if (rec) {
+        __syncthreads();
+        attn_stamp_at(rec, 3);
+    }
+}
+
 using AttnFn = void (*)(AttnParams);
+
+AttnFn pick_attn_long(int d, int kv_f16) {
+    if (d == 64) return kv_f16 ? attn_long_kernel<64, 2> : attn_long_kernel<64, 4>;
+    if (d == 128) return kv_f16 ? attn_long_kernel<128, 2> : attn_long_kernel<128, 4>;
+    return nullptr;
+}
 
 AttnFn pick_attn(int d, int kv_f16) {
     if (d == 64) return kv_f16 ? attn_kernel<64, 2> : attn_kernel<64, 4>;
@@ -343,6 +392,10 @@ int attn_smem_bytes(int head_dim, int kv_f16, int ctx_max) {
     return attn_smem_layout(head_dim, kv_f16 ? 2 : 4, attn_kv_stride(ctx_max)).total;
 }
 
+int attn_smem_bytes_long(int head_dim, int kv_f16, int ctx_max) {
+    return attn_long_smem(head_dim, kv_f16 ? 2 : 4, attn_kv_stride(ctx_max));
+}
+
 int attn_launch(const AttnLaunch &L, cudaStream_t stream) {
     AttnFn fn = pick_attn(L.head_dim, L.kv_f16);
     if (!fn) return kErrInval;
@@ -350,8 +403,13 @@ int attn_launch(const AttnLaunch &L, cudaStream_t stream) {
         return kErrInval;
     if (!L.q || !L.kcache || !L.vcache || !L.out || !L.pos) return kErrInval;
     if (reinterpret_cast<uintptr_t>(L.kcache) % 16 || reinterpret_cast<uintptr_t>(L.vcache) % 16) return kErrInval;
-    const int smem = attn_smem_bytes(L.head_dim, L.kv_f16, L.ctx_max);
-    if (smem > max_smem_optin()) return kErrInval;
+    int smem = attn_smem_bytes(L.head_dim, L.kv_f16, L.ctx_max);
+    const bool long_ctx = smem > max_smem_optin();  // the cluster's slices do not fit: the streaming kernel
+    if (long_ctx) {
+        fn = pick_attn_long(L.head_dim, L.kv_f16);
+        smem = attn_smem_bytes_long(L.head_dim, L.kv_f16, L.ctx_max);
+        if (smem > max_smem_optin()) return kErrInval;
+    }
     if (!ensure_smem(reinterpret_cast<const void *>(fn), smem)) return kErrCuda;
     AttnParams p{};
     p.q = L.q;
@@ -367,8 +425,8 @@ int attn_launch(const AttnLaunch &L, cudaStream_t stream) {
     p.scale = L.scale;
     p.trace = L.trace;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(L.kvh_local * kSplit);
-    cfg.blockDim = dim3(kAttnThreads);
+    cfg.gridDim = dim3(L.kvh_local * (long_ctx ? 1 : kSplit));
+    cfg.blockDim = dim3(long_ctx ? kLongThreads : kAttnThreads);
     cfg.dynamicSmemBytes = static_cast<size_t>(smem);
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
@@ -380,6 +438,10 @@ int attn_launch(const AttnLaunch &L, cudaStream_t stream) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = L.pdl ? 2 : 1;
+    if (long_ctx) {  // no cluster
+        cfg.attrs = attr + 1;
+        cfg.numAttrs = L.pdl ? 1 : 0;
+    }
     return cudaLaunchKernelEx(&cfg, fn, p) == cudaSuccess ? 0 : kErrCuda;
 }
 

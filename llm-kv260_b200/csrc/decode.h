@@ -33,7 +33,8 @@ int attn_kv_stride(int ctx_max);  // ctx_max rounded up to a multiple of 8
 
 // The configuration a decoder was created with (decoder.cu; for the GGUF loader).
 int decoder_config(const b200_decoder_t *d, b200_decoder_config_t *out);
-int attn_smem_bytes(int head_dim, int kv_f16, int ctx_max);
+int attn_smem_bytes(int head_dim, int kv_f16, int ctx_max);       // the cluster kernel (short contexts)
+int attn_smem_bytes_long(int head_dim, int kv_f16, int ctx_max);  // the streaming kernel it falls to
 int attn_launch(const AttnLaunch &L, cudaStream_t stream);
 
 // ------------------------------------------------------- persistent token kernel

@@ -85,6 +85,7 @@ struct b200_decoder {
     int device, rank, nranks;
     b200_comm_t *comm;
     int q_rows, kv_rows, ff_rows, vocab_rows, o_k, down_k, heads_local, kvh_local, group;
+    int o_kp;  // o_k rounded up to whole 256-column chunks: the o tiles' K, zero blocks past o_k
     cudaStream_t stream;
     std::vector<DecLayer> layers;
     std::vector<void *> allocs;
@@ -266,7 +267,7 @@ int enqueue_token(b200_decoder_t *d) {
         if (int rc = attn_launch(T, d->stream))
             return dfail(rc, "decoder: attention launch failed: %s", cudaGetErrorString(cudaGetLastError()));
 
-        TileLaunch O = gemv_base(d, W.o, e, d->o_k, d->attn, nullptr);
+        TileLaunch O = gemv_base(d, W.o, e, d->o_kp, d->attn, nullptr);
         residual_epilogue(d, O, 2 * l);
         O.trace = launch_trace(d, 5 * l + 2);
         if (int rc = launch(d, O, "o")) return rc;
@@ -396,7 +397,7 @@ int build_phases(b200_decoder_t *d) {
         TokenPhase O;
         O.w = W.o;
         O.rows = e;
-        O.k = d->o_k;
+        O.k = d->o_kp;
         O.x = d->attn;
         O.epi = kEpiResidual;
         O.ar_index = 2 * l;
@@ -533,8 +534,11 @@ extern "C" int b200_decoder_create(b200_decoder_t **out, const b200_decoder_conf
         c.n_ff % nranks || (c.round_mode != kRoundContract && c.round_mode != kRoundRoundf) || !(c.rms_eps >= 0.0f))
         return dfail(kErrInval, "decoder: unusable hyperparameters");
     const int o_k = c.n_embd / nranks, down_k = c.n_ff / nranks;
-    for (int v : {c.n_embd, o_k, down_k})
+    for (int v : {c.n_embd, down_k})
         if (v % 256 || v > kMaxK) return dfail(kErrInval, "decoder: shard width %d not a multiple of 256 up to 8192", v);
+    // attn_output's K shard may end inside a 256-column chunk (the 3B model
+    // at 8 ranks: 384 columns, 12 blocks); see set_layer
+    if (o_k % kQK || o_k > kMaxK) return dfail(kErrInval, "decoder: attn_output shard width %d unusable", o_k);
     if ((c.n_embd / nranks) % c.head_dim || (c.n_head_kv * c.head_dim / nranks) % kTileRows)
         return dfail(kErrInval, "decoder: heads do not split evenly over the ranks");
     b200_decoder_t *d = new (std::nothrow) b200_decoder_t();
@@ -549,6 +553,7 @@ extern "C" int b200_decoder_create(b200_decoder_t **out, const b200_decoder_conf
     d->ff_rows = c.n_ff / nranks;
     d->vocab_rows = c.n_vocab / nranks;
     d->o_k = o_k;
+    d->o_kp = (o_k + 255) / 256 * 256;
     d->down_k = down_k;
     d->heads_local = c.n_head / nranks;
     d->kvh_local = c.n_head_kv / nranks;
@@ -562,7 +567,8 @@ extern "C" int b200_decoder_create(b200_decoder_t **out, const b200_decoder_conf
         return rc;
     };
     if (int rc = use_dev(d)) return bail(rc);
-    if (!c.persistent && attn_smem_bytes(c.head_dim, c.kv_f16, c.ctx_max) > max_smem_optin())
+    if (!c.persistent && attn_smem_bytes(c.head_dim, c.kv_f16, c.ctx_max) > max_smem_optin() &&
+        attn_smem_bytes_long(c.head_dim, c.kv_f16, c.ctx_max) > max_smem_optin())
         return bail(dfail(kErrInval, "decoder: attention over ctx_max %d positions does not fit shared memory", c.ctx_max));
     if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess)
         return bail(dfail(kErrCuda, "decoder: stream creation failed"));
@@ -579,7 +585,7 @@ extern "C" int b200_decoder_create(b200_decoder_t **out, const b200_decoder_conf
     int rc = 0;
     if (!rc) rc = dalloc(d, &d->res, 4 * static_cast<size_t>(e));
     if (!rc) rc = dalloc(d, &d->qkv_y, 4 * static_cast<size_t>(d->q_rows + 2 * d->kv_rows));
-    if (!rc) rc = dalloc(d, &d->attn, 4 * static_cast<size_t>(o_k));
+    if (!rc) rc = dalloc(d, &d->attn, 4 * static_cast<size_t>(d->o_kp));
     if (!rc) rc = dalloc(d, &d->act, 4 * static_cast<size_t>(down_k));
     if (!rc) rc = dalloc(d, &d->act_q8, static_cast<size_t>(down_k) + 4 * static_cast<size_t>(down_k / kQK));
     if (!rc) rc = dalloc(d, &d->logits, 4 * static_cast<size_t>(d->vocab_rows));
@@ -615,6 +621,7 @@ extern "C" int b200_decoder_create(b200_decoder_t **out, const b200_decoder_conf
     cudaMemsetAsync(d->tokens, 0, 4 * (static_cast<size_t>(c.ctx_max) + 1), d->stream);
     cudaMemsetAsync(d->kv, 0, 2 * kv_bytes, d->stream);
     cudaMemsetAsync(d->res, 0, 4 * static_cast<size_t>(e), d->stream);
+    cudaMemsetAsync(d->attn, 0, 4 * static_cast<size_t>(d->o_kp), d->stream);  // the o GEMV's zero x past o_k
     // rope_table (tp_llama.cpp:574-580) for every position, on the host as the
     // reference computes it, shared with the device
     std::vector<float> cs(static_cast<size_t>(c.ctx_max) * c.head_dim);
@@ -651,10 +658,23 @@ extern "C" int b200_decoder_set_layer(b200_decoder_t *d, int layer, const void *
     append_rows(qkv, k, e, r * d->kv_rows, d->kv_rows);
     append_rows(qkv, v, e, r * d->kv_rows, d->kv_rows);
     if (int rc = upload_tiles(d, qkv, d->q_rows + 2 * d->kv_rows, e, &L.qkv)) return rc;
-    // attn_output columns (tp_llama.cpp:263-264)
-    if (int rc = upload_tiles(d, cut_cols(static_cast<const uint8_t *>(attn_output), e, e, r * d->o_k, d->o_k), e,
-                              d->o_k, &L.o))
-        return rc;
+    // attn_output columns (tp_llama.cpp:263-264). When the shard's width is
+    // not whole 256-column chunks, each row is padded with zero blocks (float16
+    // scale +0, nibbles 0) to o_kp, and the GEMV's x past o_k is zero: every
+    // padded block term is +-0, which leaves every lane sum's bits as they are
+    // (a lane starts at +0 and never holds -0), so the result is the lane rule
+    // b mod 8 applied to the shard's own blocks -- the contract extension
+    // q4_0.py:166-167 and load_model (tp_llama.cpp:247) do not allow.
+    {
+        std::vector<uint8_t> oc = cut_cols(static_cast<const uint8_t *>(attn_output), e, e, r * d->o_k, d->o_k);
+        if (d->o_kp != d->o_k) {
+            const size_t rb = row_bytes(d->o_k), pb = row_bytes(d->o_kp);
+            std::vector<uint8_t> padded(pb * e, 0);
+            for (int i = 0; i < e; ++i) memcpy(padded.data() + i * pb, oc.data() + i * rb, rb);
+            oc.swap(padded);
+        }
+        if (int rc = upload_tiles(d, oc, e, d->o_kp, &L.o)) return rc;
+    }
     // gate | up shard rows (tp_llama.cpp:266-268), stored interleaved: row 2i
     // is gate row i, row 2i+1 up row i, so each SiLU pair is a thread pair
     std::vector<uint8_t> gu;

@@ -269,7 +269,7 @@ int odec_create(odec_t **out, const odec_config_t *cfg, const odec_layer_t *laye
     d->vocab_rows = c.n_vocab / n;
     d->o_k = c.n_embd / n;
     d->down_k = c.n_ff / n;
-    if (d->o_k % 256 || d->down_k % 256) {
+    if (d->o_k % 32 || d->down_k % 256) {  /* o_k % 256: the lane-rule extension (gemv above) */
         free(d);
         return -1;
     }
@@ -347,8 +347,22 @@ int odec_create(odec_t **out, const odec_config_t *cfg, const odec_layer_t *laye
     return 0;
 }
 
+/* engine_t::gemv (tp_llama.cpp:355-374): quantize_x, then the contract's
+ * GEMV. A K-split shard whose block count is not a multiple of 8 (the 3B
+ * model's attn_output at 8 ranks: 12 blocks) uses the lane rule b mod 8 as
+ * it stands for any count -- a contract extension: q4_0.py:166-167 and
+ * load_model (tp_llama.cpp:247) refuse such shards. */
 static void gemv(const odec_t *d, const uint8_t *W, int rows, int k, const float *x, float *y) {
-    oracle_gemv_q4_0_f32(W, rows, k, x, y, d->c.threads, d->c.round_mode);
+    if (k % 256 == 0) {
+        oracle_gemv_q4_0_f32(W, rows, k, x, y, d->c.threads, d->c.round_mode);
+        return;
+    }
+    int8_t *xq = (int8_t *)malloc((size_t)k);
+    uint16_t *xd = (uint16_t *)malloc((size_t)(k / 32) * 2);
+    if (xq && xd && !oracle_quantize_q8_0(x, k, xq, xd, d->c.round_mode))
+        oracle_gemv_q4_0(W, rows, k, xq, xd, y, d->c.threads, 1);
+    free(xq);
+    free(xd);
 }
 
 /* rank-ordered all-reduce of every rank's `partial` (tp_llama.cpp:515-521),

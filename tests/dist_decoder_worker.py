@@ -100,6 +100,33 @@ def main() -> None:
             dec.close()
             comm.close()
             res["reference"][f"{name}/{mode}"] = ok
+    if world == 8:
+        # the 3B geometry at 8 ranks: attn_output's shard is 384 columns (12
+        # blocks), past what the reference's load_model accepts; the decoder
+        # pads it to whole chunks, the oracle applies the lane rule to 12
+        # blocks (the contract extension), and both must agree bit for bit
+        hp3 = dict(cases.W3B, n_vocab=4096)
+        m3 = model.synth_model(hp3, seed=53)
+        p3 = model.random_prompt(5, hp3["n_vocab"], seed=54)
+        for mode in ("graph", "persistent"):
+            comm = OrderedAllReduce(rank, world, dev, hp3["n_embd"] + 256)
+            dec = pkg.Decoder(m3, device=dev, rank=rank, nranks=world, comm=comm, ctx_max=24,
+                              persistent=mode == "persistent")
+            ref = oracle.Decoder(m3, nranks=world, ctx_max=24)
+            ok, tok = True, None
+            for i in range(20):
+                inp = int(p3[i]) if i < len(p3) else tok
+                tg, _ = dec.forward(inp, i)
+                tr, _ = ref.forward(inp, i)
+                if tg != tr or not np.array_equal(bits(dec.residual()), bits(ref.residual())):
+                    ok = f"differs at position {i}"
+                    break
+                tok = tr
+            dist.barrier()
+            dec.close()
+            comm.close()
+            ref.close()
+            res["reference"][f"w3b_r8_padded_o/{mode}"] = ok
     with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as fh:
         json.dump(res, fh)
     dist.destroy_process_group()

@@ -112,6 +112,7 @@ HD64 = dict(n_layer=2, n_embd=512, n_ff=1024, n_head=8, n_head_kv=2, head_dim=64
 HD128_G3 = dict(n_layer=2, n_embd=1536, n_ff=1536, n_head=12, n_head_kv=4, head_dim=128, n_vocab=1024,
                 rope_base=500000.0, rms_eps=1e-5)
 HD64_1L = dict(HD64, n_layer=1)
+HD128_G3_1L = dict(HD128_G3, n_layer=1)
 TPW = dict(n_layer=2, n_embd=2048, n_ff=8192, n_head=32, n_head_kv=8, head_dim=64, n_vocab=2048,
            rope_base=500000.0, rms_eps=1e-5)
 W3B = dict(n_layer=1, n_embd=3072, n_ff=8192, n_head=24, n_head_kv=8, head_dim=128, n_vocab=2048,
@@ -127,6 +128,10 @@ REF_DECODE_CASES = {
     "hd128_g3_r1_freqs": (HD128_G3, 42, 1, 5, 24, False, True),
     "hd128_g3_r2_freqs": (HD128_G3, 42, 2, 5, 24, True, True),
     "long_r1": (HD64_1L, 43, 1, 290, 300, False, False),
+    # 900 positions of float32 K/V rows at head_dim 128: past what the
+    # decoder's cluster attention holds in shared memory, so its streaming
+    # attention kernel runs
+    "hd128_long_r1": (HD128_G3_1L, 46, 1, 880, 900, False, False),
     "tpw_r4": (TPW, 44, 4, 5, 20, False, False),
     "tpw_r8": (TPW, 44, 8, 5, 20, True, False),
     "w3b_r1": (W3B, 45, 1, 5, 20, False, False),

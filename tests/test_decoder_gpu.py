@@ -206,6 +206,31 @@ def test_config3_400_greedy_tokens(cuda_lib, pkg, config3_reference, persistent)
 
 
 @pytest.mark.gpu
+def test_config5_long_context_3b_widths(cuda_lib, pkg, oracle):
+    """BASELINE config 5's attention: the 3B geometry (d_model 3072, 24 query
+    and 8 KV heads of dim 128, FFN 8192) with a float16 KV cache over a
+    4096-token prompt and 256 greedy tokens (positions up to 4351), where the
+    decoder's attention streams K and V through shared memory. One layer and
+    a 2048-token vocabulary keep the oracle's side to seconds."""
+    import cases
+    from llm_kv260_b200 import model
+    hp = dict(cases.W3B)
+    m = model.synth_model(hp, seed=51)
+    prompt = model.random_prompt(4096, hp["n_vocab"], seed=52)
+    dec = pkg.Decoder(m, ctx_max=4352)
+    toks, _, _ = dec.generate(prompt, 256)
+    ref = oracle.Decoder(m, nranks=1, ctx_max=4352)
+    want = ref.generate(prompt, 256)
+    bad = np.nonzero(np.asarray(toks) != np.asarray(want))[0]
+    assert bad.size == 0, f"first differing token at generated index {bad[0]}"
+    assert np.array_equal(bits(dec.residual()), bits(ref.residual()))
+    assert np.array_equal(bits(dec.logits()), bits(ref.logits()))
+    assert dec.status() == 0
+    dec.close()
+    ref.close()
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_tensor_parallel_decode_on_n_gpus(cuda_lib, tmp_path, world):
     """2, 4 or 8 ranks (one process per GPU) exchanging K-split partials inside

@@ -242,3 +242,41 @@ def test_gemv2_chunk_offset_is_a_bijection(oracle):
             seen[port].add(off)
     for p in range(4):
         assert sorted(seen[p]) == list(range(0, rows // 4 * row_bytes, 144))
+
+
+def test_ragged_lane_rule_equals_zero_padding(oracle):
+    """The 3B model's attn_output shard at 8 ranks has 12 blocks per row (a
+    multiple of 8 is what q4_0.py:166-167 asks). The lane rule b mod 8 applied
+    to 12 blocks gives the same bits as padding every row with zero blocks to
+    16 and x with zeros: what the GPU decoder does with that shard."""
+    w = cases.std_weights(64, 384, 31)
+    x = cases.std_weights(1, 384, 32)[0] * 3
+    blocks = oracle.quantize_q4_0(w)
+    xq, xd = oracle.quantize_q8_0(x)
+    ragged = oracle.gemv_q4_0(blocks, 384, xq, xd, allow_ragged_lanes=True)
+    pb = np.zeros((64, 512 // 32 * 18), np.uint8)
+    pb[:, : 384 // 32 * 18] = blocks
+    xp = np.zeros(512, np.float32)
+    xp[:384] = x
+    xq2, xd2 = oracle.quantize_q8_0(xp)
+    padded = oracle.gemv_q4_0(pb, 512, xq2, xd2)
+    assert np.array_equal(ragged.view(np.uint32), padded.view(np.uint32))
+    # and the lane rule itself, restated: lane b % 8 sums its blocks in order
+    qs, ds = oracle.unpack_q4_0(blocks, 384)
+    for r in (0, 17, 63):
+        lanes = np.zeros(8, np.float32)
+        for b in range(12):
+            s = int(np.dot(qs[r, 32 * b:32 * b + 32].astype(np.int64), xq[32 * b:32 * b + 32].astype(np.int64)))
+            t = np.float32(np.float32(s) * np.float32(ds[r, b])) * np.float32(xd[b])
+            lanes[b % 8] = np.float32(lanes[b % 8] + t)
+        assert np.float32(oracle.tree_sum(lanes)).view(np.uint32) == ragged[r].view(np.uint32)
+
+
+def test_decode_oracle_runs_3b_width_at_8_ranks(oracle, pkg):
+    from llm_kv260_b200 import model
+    hp = dict(cases.W3B, n_layer=1, n_vocab=256)
+    m = model.synth_model(hp, seed=9)
+    d8 = oracle.Decoder(m, nranks=8, ctx_max=8)
+    tok, val = d8.forward(3, 0)
+    assert 0 <= tok < 256 and np.isfinite(val)
+    d8.close()
