@@ -329,12 +329,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
 
 // Long contexts, where a cluster CTA's share of the head's K rows and V^T
 // columns no longer fits shared memory: one CTA per local KV head running
-// attn_core (attn_core.cuh), which streams K in 16 KB chunks and V^T in
+// attn_core (attn_core.cuh), which streams K in 8 KB chunks and V^T in
 // 256-byte column chunks through double-buffered stages -- the same
 // operations in the same order (tp_llama.cpp:644-690), so the same bits.
 constexpr int kLongThreads = 256;
 constexpr int kLongColBytes = 256;
-__host__ __device__ constexpr int long_kc(int d, int esz) { return 16384 / (d * esz); }
+__host__ __device__ constexpr int long_kc(int d, int esz) { return 8192 / (d * esz); }  // K rows per 8 KB stage
 
 __host__ __device__ inline int attn_long_smem(int d, int esz, int stride) {
     return attn_core_smem_bytes(d, esz, kLongColBytes, long_kc(d, esz), kLongThreads, stride);

@@ -46,11 +46,12 @@ namespace b200 {
 // apart (an odd number of 16-byte units, so the 32 columns a warp reads in
 // one 16-byte load fall on distinct bank groups).
 constexpr int kAttnVtStages = 2;
-constexpr int kAttnBars = kAttnVtStages + 1;  // mbarriers: V^T stages, then the K stage
+constexpr int kAttnKStages = 2;  // K chunks double-buffered: chunk c + 2 lands while chunk c + 1 is scored
+constexpr int kAttnBars = kAttnVtStages + kAttnKStages;  // mbarriers: V^T stages, then the K stages
 
 __host__ __device__ constexpr int attn_core_smem_bytes(int d, int esz, int colb, int kc, int nt, int stride) {
     return kAttnVtStages * d * (colb + 16)  // V^T stages
-           + kc * d * esz                   // K stage: kc rows
+           + kAttnKStages * kc * d * esz    // K stages: kc rows each
            + 4 * d * 4                      // q, up to 4 heads
            + (nt / 32) * 16                 // per-warp maxima, 4 heads
            + 32                             // 1 / sum per head
@@ -77,6 +78,22 @@ __device__ __forceinline__ void attn_seg_floats(const uint4 &v, float *f) {
         f[1] = __uint_as_float(v.y);
         f[2] = __uint_as_float(v.z);
         f[3] = __uint_as_float(v.w);
+    }
+}
+
+// The elements of 16 bytes of a K row that fused-multiply-add lane j
+// (0..3) takes: j and j + 4 (ESZ 2), or j (ESZ 4). Selected with j at run
+// time without indexing a register array.
+template <int ESZ>
+__device__ __forceinline__ void attn_seg_lane(const uint4 &v, int j, float *f) {
+    if constexpr (ESZ == 2) {
+        const bool hi = j & 2, odd = j & 1;
+        const uint32_t w0 = hi ? v.y : v.x, w1 = hi ? v.w : v.z;
+        f[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(odd ? w0 >> 16 : w0 & 0xffffu)));
+        f[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(odd ? w1 >> 16 : w1 & 0xffffu)));
+    } else {
+        const uint32_t w = (j & 2) ? ((j & 1) ? v.w : v.z) : ((j & 1) ? v.y : v.x);
+        f[0] = __uint_as_float(w);
     }
 }
 
@@ -136,13 +153,13 @@ __device__ bool attn_core(const float *q, const uint8_t *kb, const uint8_t *vtb,
     constexpr int kChunkPos = COLB / ESZ;  // positions per V^T chunk
     constexpr int kColStride = COLB + 16;
     constexpr int kStageBytes = D * kColStride;
-    constexpr int kKBar = kAttnVtStages;
+    constexpr int kKBar = kAttnVtStages;   // K stage s: barrier kKBar + s
     static_assert(kPer % 4 == 0 && kSegs % 8 == 0, "attention shape");
     static_assert(NT % 32 == 0 && NT >= 2 * D && KC % 8 == 0, "one thread per (column, head pair)");
 
     uint8_t *vt = smem;
     uint8_t *kbuf = smem + kAttnVtStages * kStageBytes;
-    float *qs = reinterpret_cast<float *>(kbuf + KC * kRowBytes);
+    float *qs = reinterpret_cast<float *>(kbuf + kAttnKStages * KC * kRowBytes);
     float *part = qs + 4 * D;             // [NT/32][4]
     float *hinv = part + (NT / 32) * 4;   // [4] 1 / sum per head, then a failure flag
     int *fail = reinterpret_cast<int *>(hinv + 4);
@@ -168,15 +185,16 @@ __device__ bool attn_core(const float *q, const uint8_t *kb, const uint8_t *vtb,
                      vtb + static_cast<size_t>(tid) * stride * ESZ + static_cast<size_t>(c) * COLB, colb, &bars[slot], pol);
         pend |= 1u << slot;
     };
-    // K rows [kc * KC, ...) into the K stage: one copy
+    // K rows [kc * KC, ...) into K stage kc % 2: one copy
     auto stage_k = [&](int kc) {
-        const int r0 = kc * KC, rows = min(KC, n - r0);
+        if (kc >= nkc) return;
+        const int r0 = kc * KC, rows = min(KC, n - r0), sb = kKBar + kc % kAttnKStages;
         if (tid == 0) {
-            mbar_arrive_expect_tx(&bars[kKBar], static_cast<uint32_t>(rows * kRowBytes));
-            bulk_g2s(kbuf, kb + static_cast<size_t>(r0) * kRowBytes, static_cast<uint32_t>(rows * kRowBytes), &bars[kKBar],
-                     pol);
+            mbar_arrive_expect_tx(&bars[sb], static_cast<uint32_t>(rows * kRowBytes));
+            bulk_g2s(kbuf + (kc % kAttnKStages) * KC * kRowBytes, kb + static_cast<size_t>(r0) * kRowBytes,
+                     static_cast<uint32_t>(rows * kRowBytes), &bars[sb], pol);
         }
-        pend |= 1u << kKBar;
+        pend |= 1u << sb;
     };
     auto wait_bar = [&](int b) {
         if (wait_stage(&bars[b], (par >> b) & 1u, status)) {
@@ -204,6 +222,7 @@ __device__ bool attn_core(const float *q, const uint8_t *kb, const uint8_t *vtb,
         if (i < G * D) qv[u] = __ldcg(q + i);
     }
     stage_k(0);
+    stage_k(1);
 #pragma unroll
     for (int u = 0; u < (4 * D + NT - 1) / NT; ++u) {
         const int i = tid + u * NT;
@@ -217,17 +236,23 @@ __device__ bool attn_core(const float *q, const uint8_t *kb, const uint8_t *vtb,
     stage_vt(0);
     stage_vt(1);
 
-    // scores (tp_llama.cpp:652-664) and this thread's maxima
+    // scores (tp_llama.cpp:652-664) and this thread's maxima: four threads
+    // per position, thread j running fused-multiply-add lane j (elements
+    // i = j, j+4, ... in order) of every head; the lanes meet as
+    // (l0 + l1) + (l2 + l3) by xor shuffles 1 then 2 -- vaddvq_f32's pairing,
+    // so all four threads hold the reference's score
     float mx[4] = {-1e30f, -1e30f, -1e30f, -1e30f};
+    const int jl = tid & 3;
     for (int kc = 0; kc < nkc; ++kc) {
         const int r0 = kc * KC, r1 = min(n, r0 + KC);
-        wait_bar(kKBar);
-        for (int t = r0 + tid; t < r1; t += NT) {
-            const uint8_t *row = kbuf + (t - r0) * kRowBytes;
+        wait_bar(kKBar + kc % kAttnKStages);
+        const uint8_t *kst = kbuf + (kc % kAttnKStages) * KC * kRowBytes;
+        for (int t0 = r0; t0 < r1; t0 += NT / 4) {  // the same trip count in every thread
+            const int t = t0 + (tid >> 2);
+            const bool live = t < r1;
+            const uint8_t *row = kst + (live ? t - r0 : 0) * kRowBytes;
             const int sw = t & 7;
-            float a[4][4];
-#pragma unroll
-            for (int b = 0; b < 4; ++b) a[b][0] = a[b][1] = a[b][2] = a[b][3] = 0.0f;
+            float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
             for (int s8 = 0; s8 < kSegs; s8 += 8) {
                 uint4 kr[8];
@@ -235,20 +260,15 @@ __device__ bool attn_core(const float *q, const uint8_t *kb, const uint8_t *vtb,
                 for (int j = 0; j < 8; ++j) kr[j] = *reinterpret_cast<const uint4 *>(row + (s8 + (j ^ sw)) * 16);
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    float f[8];
-                    attn_seg_floats<ESZ>(kr[j], f);
+                    float f[kPer / 4];
+                    attn_seg_lane<ESZ>(kr[j], jl, f);
                     const int i0 = (s8 + j) * kPer;
 #pragma unroll
                     for (int b = 0; b < 4; ++b) {
                         if (b < G) {
 #pragma unroll
-                            for (int m4 = 0; m4 < kPer; m4 += 4) {
-                                const float4 qv4 = lds_f4(qs + b * D + i0 + m4);
-                                a[b][0] = __fmaf_rn(f[m4], qv4.x, a[b][0]);
-                                a[b][1] = __fmaf_rn(f[m4 + 1], qv4.y, a[b][1]);
-                                a[b][2] = __fmaf_rn(f[m4 + 2], qv4.z, a[b][2]);
-                                a[b][3] = __fmaf_rn(f[m4 + 3], qv4.w, a[b][3]);
-                            }
+                            for (int u = 0; u < kPer / 4; ++u)
+                                a[b] = __fmaf_rn(f[u], qs[b * D + i0 + 4 * u + jl], a[b]);
                         }
                     }
                 }
@@ -257,16 +277,17 @@ __device__ bool attn_core(const float *q, const uint8_t *kb, const uint8_t *vtb,
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
                 if (b < G) {
-                    sv[b] = __fmul_rn(__fadd_rn(__fadd_rn(a[b][0], a[b][1]), __fadd_rn(a[b][2], a[b][3])), scale);
-                    mx[b] = attn_max_gt(mx[b], sv[b]);
+                    const float x = __fadd_rn(a[b], __shfl_xor_sync(kFullMask, a[b], 1));
+                    sv[b] = __fmul_rn(__fadd_rn(x, __shfl_xor_sync(kFullMask, x, 2)), scale);
+                    if (live) mx[b] = attn_max_gt(mx[b], sv[b]);
                 }
             }
-            e[t] = make_float4(sv[0], sv[1], sv[2], sv[3]);
+            if (live && jl == 0) e[t] = make_float4(sv[0], sv[1], sv[2], sv[3]);
         }
         if (kc + 1 < nkc) {
-            named_sync(bar, NT);  // the K stage consumed
+            named_sync(bar, NT);  // K stage kc % 2 consumed
             if (*reinterpret_cast<volatile int *>(fail)) return drain();
-            stage_k(kc + 1);
+            stage_k(kc + 2);
         }
     }
 #pragma unroll

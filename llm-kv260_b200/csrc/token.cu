@@ -608,7 +608,7 @@ __device__ void gemv_phase(const MkParams &p, const TokenPhase &ph, const PhaseC
 // ------------------------------------------------------------------ attention
 
 constexpr int kAttnColBytes = 256;  // V^T bytes per column per chunk (attn_core.cuh)
-__host__ __device__ constexpr int mk_attn_kc(int d, int esz) { return 16384 / (d * esz); }  // K rows per chunk: 16 KB
+__host__ __device__ constexpr int mk_attn_kc(int d, int esz) { return 8192 / (d * esz); }  // K rows per stage: 8 KB
 
 // attention_group (tp_llama.cpp:644-690) for KV head `kvh` = this CTA's
 // index, over positions 0..P: attn_core, which states the order of every
