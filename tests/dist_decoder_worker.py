@@ -27,6 +27,10 @@ def bits(a) -> np.ndarray:
     return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
 
 
+# every rank runs its own oracle on the same host: share the cores
+ORACLE_THREADS = max(1, (os.cpu_count() or 1) // int(os.environ.get("WORLD_SIZE", "1")))
+
+
 def main() -> None:
     out_dir = sys.argv[1]
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
@@ -46,7 +50,7 @@ def main() -> None:
         comm = OrderedAllReduce(rank, world, dev, TPW["n_embd"] + 256)
         dec = pkg.Decoder(m, device=dev, rank=rank, nranks=world, comm=comm, ctx_max=48,
                           persistent=mode == "persistent")
-        ref = oracle.Decoder(m, nranks=world, ctx_max=48)
+        ref = oracle.Decoder(m, nranks=world, ctx_max=48, threads=ORACLE_THREADS)
         tok = None
         for i in range(14):
             inp = int(prompt[i]) if i < len(prompt) else tok
@@ -60,7 +64,7 @@ def main() -> None:
                 r["first_bad_position"] = i
                 break
             tok = tr
-        ref2 = oracle.Decoder(m, nranks=world, ctx_max=48)
+        ref2 = oracle.Decoder(m, nranks=world, ctx_max=48, threads=ORACLE_THREADS)
         want = ref2.generate(prompt, 30)
         got, _, _ = dec.generate(prompt, 30)
         r["generate"] = list(map(int, got)) == list(map(int, want))
@@ -112,7 +116,7 @@ def main() -> None:
             comm = OrderedAllReduce(rank, world, dev, hp3["n_embd"] + 256)
             dec = pkg.Decoder(m3, device=dev, rank=rank, nranks=world, comm=comm, ctx_max=24,
                               persistent=mode == "persistent")
-            ref = oracle.Decoder(m3, nranks=world, ctx_max=24)
+            ref = oracle.Decoder(m3, nranks=world, ctx_max=24, threads=ORACLE_THREADS)
             ok, tok = True, None
             for i in range(20):
                 inp = int(p3[i]) if i < len(p3) else tok
