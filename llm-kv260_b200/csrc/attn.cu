@@ -327,54 +327,326 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
     }
 }
 
-// Long contexts, where a cluster CTA's share of the head's K rows and V^T
-// columns no longer fits shared memory: one CTA per local KV head running
-// attn_core (attn_core.cuh), which streams K in 8 KB chunks and V^T in
-// 256-byte column chunks through double-buffered stages -- the same
-// operations in the same order (tp_llama.cpp:644-690), so the same bits.
-constexpr int kLongThreads = 256;
-constexpr int kLongColBytes = 256;
-__host__ __device__ constexpr int long_kc(int d, int esz) { return 8192 / (d * esz); }  // K rows per 8 KB stage
+// Long contexts, cluster form: the cluster kernel's split (CTA r scores a
+// quarter of the positions and chains a quarter of the columns) with K and
+// V^T streamed through rings of shared-memory stages instead of held whole.
+//   scores  4 threads per position (fused-multiply-add lane j each, met by
+//           xor shuffles 1 then 2: vaddvq_f32's pairing); every score row to
+//           all four CTAs (distributed shared memory); one cluster barrier;
+//   softmax each CTA: maxima, v_expf, the four sequential lane sums per head
+//           read from a lane-major copy of the exponentials, 1 / sum, p;
+//   output  one thread per (column, head): the fused-multiply-add chain over
+//           t = 0..n-1 in order, chunk by chunk.
+// The V^T ring reuses the K ring's shared memory and starts filling as soon
+// as the scores are done, behind the softmax.
+constexpr int kStreamThreads = 256;
+constexpr int kStreamKStages = 4;
+constexpr int kStreamVStages = 3;
+constexpr int kStreamColBytes = 512;  // V^T bytes of a column per stage
 
-__host__ __device__ inline int attn_long_smem(int d, int esz, int stride) {
-    return attn_core_smem_bytes(d, esz, kLongColBytes, long_kc(d, esz), kLongThreads, stride);
+struct StreamSmem {
+    int e, pt, ring, qs, part, hinv, total;
+    int krows;     // K rows per stage
+    int vcol;      // bytes between two V^T columns of a stage (odd number of 16-byte units)
+    int vstage;    // bytes of a V^T stage
+};
+
+__host__ __device__ inline StreamSmem stream_smem_layout(int d, int esz, int stride) {
+    StreamSmem L{};
+    L.krows = 16384 / (d * esz);  // 16 KB per K stage
+    L.vcol = kStreamColBytes + 16;
+    L.vstage = (d / kSplit) * L.vcol;
+    const int kring = kStreamKStages * L.krows * d * esz, vring = kStreamVStages * L.vstage;
+    int off = 0;
+    auto carve = [&](int bytes) {
+        const int at = off;
+        off += (bytes + 15) / 16 * 16;
+        return at;
+    };
+    L.e = carve(16 * stride);
+    L.pt = carve(16 * stride);
+    L.ring = carve(kring > vring ? kring : vring);
+    L.qs = carve(4 * d * 4);
+    L.part = carve((kStreamThreads / 32) * 16);
+    L.hinv = carve(32);
+    L.total = off;
+    return L;
 }
 
 template <int D, int ESZ>
-__global__ void __launch_bounds__(kLongThreads, 1) attn_long_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(kStreamThreads, 1) attn_stream_kernel(const __grid_constant__ AttnParams p) {
+    constexpr int kRowBytes = D * ESZ;
+    constexpr int kSegs = kRowBytes / 16;
+    constexpr int kPer = 16 / ESZ;
+    constexpr int CW = D / kSplit;
+    constexpr int kChunkPos = kStreamColBytes / ESZ;  // positions per V^T stage
+    constexpr int NT = kStreamThreads;
+    constexpr int kQv = (4 * D + NT - 1) / NT;
+    static_assert(kSegs % 8 == 0 && kPer % 4 == 0 && 4 * CW <= NT, "attention shape");
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t bars[kAttnBars];
-    const int kvh = blockIdx.x;
+    __shared__ uint64_t kbar[kStreamKStages], vbar[kStreamVStages];
+    __shared__ int s_fail;
+    const StreamSmem S = stream_smem_layout(D, ESZ, p.stride);
+    float4 *e = reinterpret_cast<float4 *>(smem + S.e);   // [position]: 4 heads' scores, then exponentials
+    float *pt = reinterpret_cast<float *>(smem + S.pt);    // exponentials lane-major, then p [head][position]
+    uint8_t *ring = smem + S.ring;
+    float *qs = reinterpret_cast<float *>(smem + S.qs);
+    float *part = reinterpret_cast<float *>(smem + S.part);
+    float *hinv = reinterpret_cast<float *>(smem + S.hinv);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, G = p.group, KC = S.krows;
+    const int kvh = blockIdx.x / kSplit;
+    const int r = static_cast<int>(cluster_ctarank());
+    const int c0 = r * CW;
+    const size_t head_bytes = static_cast<size_t>(p.stride) * D * ESZ;
+    const uint8_t *kb = p.kcache + kvh * head_bytes;
+    const uint8_t *vtb = p.vcache + kvh * head_bytes;
     uint64_t *rec = attn_rec(p.trace);
-    if (threadIdx.x == 0) {
-        for (int b = 0; b < kAttnBars; ++b) mbar_init(&bars[b], 1);
+    if (tid == 0) {
+        for (int i = 0; i < kStreamKStages; ++i) mbar_init(&kbar[i], 1);
+        for (int i = 0; i < kStreamVStages; ++i) mbar_init(&vbar[i], 1);
         fence_mbar_init();
+        s_fail = 0;
     }
     __syncthreads();
     pdl_launch_dependents();
     attn_stamp_at(rec, 0);
+    cluster_sync_all();  // every CTA of the cluster runs before any store into its shared memory
     pdl_wait_prior_grid();
     attn_stamp_at(rec, 1);
+
     const int n = *p.pos + 1;
-    const size_t head_bytes = static_cast<size_t>(p.stride) * D * ESZ;
-    uint32_t par = 0;
-    if (!attn_core<D, ESZ, kLongColBytes, long_kc(D, ESZ), kLongThreads>(
-            p.q + static_cast<size_t>(kvh) * p.group * D, p.kcache + kvh * head_bytes, p.vcache + kvh * head_bytes,
-            p.stride, n, p.group, p.scale, p.out + static_cast<size_t>(kvh) * p.group * D, smem, 1, bars, par, p.status,
-            rec) &&
-        threadIdx.x == 0)
-        atomicOr(p.status, kStatusStageTimeout);
-    if (rec) {
-        __syncthreads();
-        attn_stamp_at(rec, 3);
+    const int per = (n + kSplit - 1) / kSplit;
+    const int r0 = min(n, r * per), r1 = min(n, r0 + per);
+    const int nk = (r1 - r0 + KC - 1) / KC;
+    const int nv = (n + kChunkPos - 1) / kChunkPos;
+    const uint64_t pol = l2_policy_evict_last();
+    auto stage_k = [&](int kc) {  // K rows [r0 + kc * KC, ...) into stage kc % KS (thread 0)
+        if (kc >= nk) return;
+        const int a = r0 + kc * KC, rows = min(KC, r1 - a), st = kc % kStreamKStages;
+        const uint32_t bytes = static_cast<uint32_t>(rows * kRowBytes);
+        mbar_arrive_expect_tx(&kbar[st], bytes);
+        bulk_g2s(ring + st * KC * kRowBytes, kb + static_cast<size_t>(a) * kRowBytes, bytes, &kbar[st], pol);
+    };
+    auto stage_v = [&](int c) {  // V^T positions [c * CP, ...) of this CTA's columns into stage c % VS (threads < CW)
+        if (c >= nv) return;
+        const int rows = min(kChunkPos, n - c * kChunkPos), st = c % kStreamVStages;
+        const uint32_t colb = static_cast<uint32_t>((rows * ESZ + 15) / 16 * 16);  // stays below stride: stride % 8 == 0
+        if (tid == 0) mbar_arrive_expect_tx(&vbar[st], colb * CW);
+        __syncwarp();
+        if (tid < CW)
+            bulk_g2s(ring + st * S.vstage + tid * S.vcol,
+                     vtb + static_cast<size_t>(c0 + tid) * p.stride * ESZ + static_cast<size_t>(c) * kStreamColBytes, colb,
+                     &vbar[st], pol);
+    };
+    // q first (the critical path), then the first K stages
+    float qv[kQv];
+#pragma unroll
+    for (int u = 0; u < kQv; ++u) {
+        const int i = tid + u * NT;
+        if (i < G * D) qv[u] = __ldcg(p.q + static_cast<size_t>(kvh) * G * D + i);
     }
+    if (tid == 0)
+        for (int kc = 0; kc < kStreamKStages; ++kc) stage_k(kc);
+#pragma unroll
+    for (int u = 0; u < kQv; ++u) {
+        const int i = tid + u * NT;
+        if (i < G * D) qs[i] = qv[u];
+    }
+    __syncthreads();
+    attn_stamp_at(rec, 4);
+
+    // scores of positions [r0, r1) (tp_llama.cpp:652-664), to every CTA
+    const int jl = tid & 3;
+    for (int kc = 0; kc < nk; ++kc) {
+        const int a0 = r0 + kc * KC, a1 = min(r1, a0 + KC), st = kc % kStreamKStages;
+        if (!s_fail && !wait_stage(&kbar[st], static_cast<uint32_t>((kc / kStreamKStages) & 1), p.status))
+            atomicExch(&s_fail, 1);
+        const uint8_t *kst = ring + st * KC * kRowBytes;
+        for (int t0 = a0; t0 < a1; t0 += NT / 4) {  // the same trip count in every thread
+            const int t = t0 + (tid >> 2);
+            const bool live = t < a1;
+            const uint8_t *row = kst + (live ? t - a0 : 0) * kRowBytes;
+            const int sw = t & 7;
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int s8 = 0; s8 < kSegs; s8 += 8) {
+                uint4 kr[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) kr[j] = *reinterpret_cast<const uint4 *>(row + (s8 + (j ^ sw)) * 16);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    float f[kPer / 4];
+                    attn_seg_lane<ESZ>(kr[j], jl, f);
+                    const int i0 = (s8 + j) * kPer;
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        if (b < G) {
+#pragma unroll
+                            for (int u = 0; u < kPer / 4; ++u)
+                                acc[b] = __fmaf_rn(f[u], qs[b * D + i0 + 4 * u + jl], acc[b]);
+                        }
+                    }
+                }
+            }
+            float sv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const float x = __fadd_rn(acc[b], __shfl_xor_sync(kFullMask, acc[b], 1));
+                if (b < G) sv[b] = __fmul_rn(__fadd_rn(x, __shfl_xor_sync(kFullMask, x, 2)), p.scale);
+            }
+            if (live && jl < kSplit)  // the four lanes hold the same row: lane j writes CTA j's copy
+                st_cluster_f4(cluster_map(&e[t], static_cast<uint32_t>(jl)), make_float4(sv[0], sv[1], sv[2], sv[3]));
+        }
+        __syncthreads();  // stage consumed
+        if (tid == 0) stage_k(kc + kStreamKStages);
+    }
+    // the K ring is done: the V^T stages fill it behind the softmax
+    if (!s_fail)
+        for (int c = 0; c < kStreamVStages; ++c) stage_v(c);
+    cluster_sync_all();  // every CTA now holds all n scores
+    attn_stamp_at(rec, 5);
+
+    // running max per head over all positions (exact: any tree of `>` gives
+    // the reference's value), then the exponentials -- into e, and lane-major
+    // into pt for the sums: exponential of position 4u + j, head b at
+    // pt[(4 b + j) * (stride / 4) + u]
+    float mx[4] = {-1e30f, -1e30f, -1e30f, -1e30f};
+    for (int t = tid; t < n; t += NT) {
+        const float4 sc = e[t];
+        mx[0] = attn_max_gt(mx[0], sc.x);
+        mx[1] = attn_max_gt(mx[1], sc.y);
+        mx[2] = attn_max_gt(mx[2], sc.z);
+        mx[3] = attn_max_gt(mx[3], sc.w);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) mx[b] = attn_max_gt(mx[b], __shfl_xor_sync(kFullMask, mx[b], off));
+    }
+    if (lane == 0) *reinterpret_cast<float4 *>(part + warp * 4) = make_float4(mx[0], mx[1], mx[2], mx[3]);
+    __syncthreads();
+    float m[4] = {-1e30f, -1e30f, -1e30f, -1e30f};
+    for (int w = 0; w < NT / 32; ++w) {
+        const float4 pw = *reinterpret_cast<const float4 *>(part + w * 4);
+        m[0] = attn_max_gt(m[0], pw.x);
+        m[1] = attn_max_gt(m[1], pw.y);
+        m[2] = attn_max_gt(m[2], pw.z);
+        m[3] = attn_max_gt(m[3], pw.w);
+    }
+    const int q4 = p.stride / 4;
+    for (int t = tid; t < n; t += NT) {
+        float4 sc = e[t];
+        sc.x = v_expf(__fsub_rn(sc.x, m[0]));
+        if (G > 1) sc.y = v_expf(__fsub_rn(sc.y, m[1]));
+        if (G > 2) sc.z = v_expf(__fsub_rn(sc.z, m[2]));
+        if (G > 3) sc.w = v_expf(__fsub_rn(sc.w, m[3]));
+        e[t] = sc;
+        const int j = t & 3, u = t >> 2;
+        pt[(0 + j) * q4 + u] = sc.x;
+        pt[(4 + j) * q4 + u] = sc.y;
+        pt[(8 + j) * q4 + u] = sc.z;
+        pt[(12 + j) * q4 + u] = sc.w;
+    }
+    __syncthreads();
+    attn_stamp_at(rec, 6);
+
+    // sums (softmax_exp, tp_llama.cpp:626-633): warp 0, lane 4 * head + j
+    // adds positions j, j+4, ... below n - n % 4 in order, reading its lane's
+    // row of pt 16 bytes at a time; (l0 + l1) + (l2 + l3) by two xor
+    // shuffles; then the tail one by one; inv = 1 / sum
+    if (warp == 0) {
+        const int b = lane >> 2, j4 = lane & 3, n4 = n & ~3, nu = n4 / 4;
+        const float *row = pt + (4 * b + j4) * q4;
+        float acc = 0.0f;
+        if (b < G) {
+            int u = 0;
+            const bool al = (q4 & 3) == 0;  // rows 16-byte aligned: q4 % 4 == 0 (stride % 16 == 0)
+            if (al) {
+#pragma unroll 4
+                for (; u + 4 <= nu; u += 4) {
+                    const float4 v4 = *reinterpret_cast<const float4 *>(row + u);
+                    acc = __fadd_rn(acc, v4.x);
+                    acc = __fadd_rn(acc, v4.y);
+                    acc = __fadd_rn(acc, v4.z);
+                    acc = __fadd_rn(acc, v4.w);
+                }
+            }
+            for (; u < nu; ++u) acc = __fadd_rn(acc, row[u]);
+        }
+        const float x = __fadd_rn(acc, __shfl_xor_sync(kFullMask, acc, 1));
+        const float y = __fadd_rn(x, __shfl_xor_sync(kFullMask, x, 2));
+        if (b < G && j4 == 0) {
+            float sum = y;
+            const float *col = reinterpret_cast<const float *>(e) + b;
+            for (int t = n4; t < n; ++t) sum = __fadd_rn(sum, col[4 * t]);
+            hinv[b] = __frcp_rn(sum);  // IEEE 1 / sum, round to nearest: the reference's 1.0f / sum
+        }
+    }
+    __syncthreads();
+    attn_stamp_at(rec, 7);
+    // p_t = s_t * inv (tp_llama.cpp:680), per head contiguous (over pt: the sums are done)
+    {
+        const float4 iv = *reinterpret_cast<const float4 *>(hinv);
+        for (int t = tid; t < n; t += NT) {
+            const float4 sc = e[t];
+            pt[t] = __fmul_rn(sc.x, iv.x);
+            if (G > 1) pt[p.stride + t] = __fmul_rn(sc.y, iv.y);
+            if (G > 2) pt[2 * p.stride + t] = __fmul_rn(sc.z, iv.z);
+            if (G > 3) pt[3 * p.stride + t] = __fmul_rn(sc.w, iv.w);
+        }
+    }
+    __syncthreads();
+    attn_stamp_at(rec, 2);
+
+    // output chains (tp_llama.cpp:667-687): thread (column c0 + j, head h),
+    // acc = fma(v[t][c], p_t, acc) for t = 0..n-1 in order, stage by stage
+    const int j = tid % CW, h = tid / CW;
+    const bool chain = h < G;
+    float acc = 0.0f;
+    for (int c = 0; c < nv; ++c) {
+        const int st = c % kStreamVStages;
+        if (!s_fail && !wait_stage(&vbar[st], static_cast<uint32_t>((c / kStreamVStages) & 1), p.status))
+            atomicExch(&s_fail, 1);
+        if (chain && !s_fail) {
+            const uint8_t *vc = ring + st * S.vstage + j * S.vcol;
+            const float *ph = pt + h * p.stride + c * kChunkPos;
+            const int rows = min(kChunkPos, n - c * kChunkPos), full = rows / kPer * kPer;
+            int t = 0;
+#pragma unroll 8
+            for (; t < full; t += kPer) {
+                const uint4 vr = *reinterpret_cast<const uint4 *>(vc + t * ESZ);
+                float v[8];
+                attn_seg_floats<ESZ>(vr, v);
+#pragma unroll
+                for (int k4 = 0; k4 < kPer; k4 += 4) {
+                    const float4 p4 = *reinterpret_cast<const float4 *>(ph + t + k4);
+                    acc = __fmaf_rn(v[k4], p4.x, acc);
+                    acc = __fmaf_rn(v[k4 + 1], p4.y, acc);
+                    acc = __fmaf_rn(v[k4 + 2], p4.z, acc);
+                    acc = __fmaf_rn(v[k4 + 3], p4.w, acc);
+                }
+            }
+            for (; t < rows; ++t) acc = __fmaf_rn(attn_elem<ESZ>(vc, t), ph[t], acc);
+        }
+        __syncthreads();  // stage consumed
+        if (!s_fail) stage_v(c + kStreamVStages);
+    }
+    if (chain && !s_fail) p.out[(static_cast<size_t>(kvh) * G + h) * D + c0 + j] = acc;
+    if (s_fail && tid == 0) {
+        // a wait ran out: let this CTA's copies in flight land (each wait
+        // bounded) before its shared memory goes away
+        for (int i = 0; i < kStreamKStages; ++i) (void)wait_stage(&kbar[i], 0u, p.status), (void)wait_stage(&kbar[i], 1u, p.status);
+        for (int i = 0; i < kStreamVStages; ++i) (void)wait_stage(&vbar[i], 0u, p.status), (void)wait_stage(&vbar[i], 1u, p.status);
+    }
+    __syncthreads();
+    attn_stamp_at(rec, 3);
 }
 
 using AttnFn = void (*)(AttnParams);
 
-AttnFn pick_attn_long(int d, int kv_f16) {
-    if (d == 64) return kv_f16 ? attn_long_kernel<64, 2> : attn_long_kernel<64, 4>;
-    if (d == 128) return kv_f16 ? attn_long_kernel<128, 2> : attn_long_kernel<128, 4>;
+AttnFn pick_attn_stream(int d, int kv_f16) {
+    if (d == 64) return kv_f16 ? attn_stream_kernel<64, 2> : attn_stream_kernel<64, 4>;
+    if (d == 128) return kv_f16 ? attn_stream_kernel<128, 2> : attn_stream_kernel<128, 4>;
     return nullptr;
 }
 
@@ -393,7 +665,7 @@ int attn_smem_bytes(int head_dim, int kv_f16, int ctx_max) {
 }
 
 int attn_smem_bytes_long(int head_dim, int kv_f16, int ctx_max) {
-    return attn_long_smem(head_dim, kv_f16 ? 2 : 4, attn_kv_stride(ctx_max));
+    return stream_smem_layout(head_dim, kv_f16 ? 2 : 4, attn_kv_stride(ctx_max)).total;
 }
 
 int attn_launch(const AttnLaunch &L, cudaStream_t stream) {
@@ -406,7 +678,7 @@ int attn_launch(const AttnLaunch &L, cudaStream_t stream) {
     int smem = attn_smem_bytes(L.head_dim, L.kv_f16, L.ctx_max);
     const bool long_ctx = smem > max_smem_optin();  // the cluster's slices do not fit: the streaming kernel
     if (long_ctx) {
-        fn = pick_attn_long(L.head_dim, L.kv_f16);
+        fn = pick_attn_stream(L.head_dim, L.kv_f16);
         smem = attn_smem_bytes_long(L.head_dim, L.kv_f16, L.ctx_max);
         if (smem > max_smem_optin()) return kErrInval;
     }
@@ -425,8 +697,8 @@ int attn_launch(const AttnLaunch &L, cudaStream_t stream) {
     p.scale = L.scale;
     p.trace = L.trace;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(L.kvh_local * (long_ctx ? 1 : kSplit));
-    cfg.blockDim = dim3(long_ctx ? kLongThreads : kAttnThreads);
+    cfg.gridDim = dim3(L.kvh_local * kSplit);
+    cfg.blockDim = dim3(long_ctx ? kStreamThreads : kAttnThreads);
     cfg.dynamicSmemBytes = static_cast<size_t>(smem);
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
@@ -438,10 +710,6 @@ int attn_launch(const AttnLaunch &L, cudaStream_t stream) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = L.pdl ? 2 : 1;
-    if (long_ctx) {  // no cluster
-        cfg.attrs = attr + 1;
-        cfg.numAttrs = L.pdl ? 1 : 0;
-    }
     return cudaLaunchKernelEx(&cfg, fn, p) == cudaSuccess ? 0 : kErrCuda;
 }
 
