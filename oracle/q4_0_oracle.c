@@ -68,34 +68,50 @@ static pthread_mutex_t pool_busy = PTHREAD_MUTEX_INITIALIZER;   /* held by the p
 static pthread_mutex_t pool_mu = PTHREAD_MUTEX_INITIALIZER;
 static pthread_cond_t pool_cv = PTHREAD_COND_INITIALIZER;
 static int pool_workers;                  /* started so far (never stopped) */
-static _Atomic unsigned pool_gen;         /* job number, bumped per call */
-static _Atomic int pool_left;             /* spans of the current job not yet done */
+/* The current job as one word: job number << 32 | span count << 16 | next
+ * unclaimed span. A thread claims span i by moving the word from i to i + 1
+ * (compare-and-swap), so a claim always names a span of the job that word
+ * describes, and every span is run exactly once. The span table is written
+ * only between jobs: the caller rewrites it after every span of the previous
+ * job has finished (pool_left == 0), and a claim of the new job succeeds
+ * only after the word announces it. */
+static _Atomic uint64_t pool_claim;
+static _Atomic int pool_left;             /* claimed-or-not spans of the current job not yet finished */
 static span_t pool_span[POOL_MAX];
-static int pool_nspans;
-static unsigned pool_gen0[POOL_MAX];      /* the job number when worker i started */
+
+/* Run spans of the current job until none is left to claim. */
+static void pool_drain(void) {
+    for (;;) {
+        uint64_t w = atomic_load_explicit(&pool_claim, memory_order_acquire);
+        const uint32_t next = (uint32_t)(w & 0xffffu), ns = (uint32_t)((w >> 16) & 0xffffu);
+        if (next >= ns) return;
+        if (!atomic_compare_exchange_weak_explicit(&pool_claim, &w, w + 1, memory_order_acq_rel, memory_order_acquire))
+            continue;
+        const span_t *sp = &pool_span[next];
+        sp->fn(sp->ctx, sp->lo, sp->hi);
+        atomic_fetch_sub_explicit(&pool_left, 1, memory_order_acq_rel);
+    }
+}
 
 static void *pool_worker(void *arg) {
-    const int id = (int)(intptr_t)arg; /* 1 .. */
-    unsigned seen = pool_gen0[id];
+    (void)arg;
+    uint32_t seen = (uint32_t)(atomic_load_explicit(&pool_claim, memory_order_acquire) >> 32);
     for (;;) {
-        unsigned g;
+        uint32_t g;
         int spins = 0;
-        while ((g = atomic_load_explicit(&pool_gen, memory_order_acquire)) == seen) {
+        while ((g = (uint32_t)(atomic_load_explicit(&pool_claim, memory_order_acquire) >> 32)) == seen) {
             if (++spins < 20000) {
                 sched_yield();
                 continue;
             }
             pthread_mutex_lock(&pool_mu);
-            while ((g = atomic_load_explicit(&pool_gen, memory_order_acquire)) == seen) pthread_cond_wait(&pool_cv, &pool_mu);
+            while ((g = (uint32_t)(atomic_load_explicit(&pool_claim, memory_order_acquire) >> 32)) == seen)
+                pthread_cond_wait(&pool_cv, &pool_mu);
             pthread_mutex_unlock(&pool_mu);
             break;
         }
         seen = g;
-        if (id < pool_nspans) {
-            const span_t *s = &pool_span[id];
-            s->fn(s->ctx, s->lo, s->hi);
-            atomic_fetch_sub_explicit(&pool_left, 1, memory_order_acq_rel);
-        }
+        pool_drain();
     }
     return NULL;
 }
@@ -110,25 +126,23 @@ static void parallel_rows(int64_t n, int threads, void (*fn)(void *, int64_t, in
     }
     while (pool_workers < threads - 1) {
         pthread_t tid;
-        pool_gen0[pool_workers + 1] = atomic_load(&pool_gen);
-        if (pthread_create(&tid, NULL, pool_worker, (void *)(intptr_t)(pool_workers + 1))) break;
+        if (pthread_create(&tid, NULL, pool_worker, NULL)) break;
         pthread_detach(tid);
         ++pool_workers;
     }
-    if (threads > pool_workers + 1) threads = pool_workers + 1;
     for (int t = 0; t < threads; ++t) {
         pool_span[t].fn = fn;
         pool_span[t].ctx = ctx;
         pool_span[t].lo = n * t / threads;
         pool_span[t].hi = n * (t + 1) / threads;
     }
-    pool_nspans = threads;
-    atomic_store_explicit(&pool_left, threads - 1, memory_order_relaxed);
+    atomic_store_explicit(&pool_left, threads, memory_order_relaxed);
+    const uint64_t g = (atomic_load_explicit(&pool_claim, memory_order_relaxed) >> 32) + 1;
     pthread_mutex_lock(&pool_mu);
-    atomic_fetch_add_explicit(&pool_gen, 1u, memory_order_release);
+    atomic_store_explicit(&pool_claim, (g << 32) | ((uint64_t)threads << 16), memory_order_release);
     pthread_cond_broadcast(&pool_cv);
     pthread_mutex_unlock(&pool_mu);
-    fn(ctx, pool_span[0].lo, pool_span[0].hi);
+    pool_drain();  /* the caller takes spans too */
     while (atomic_load_explicit(&pool_left, memory_order_acquire) > 0) sched_yield();
     pthread_mutex_unlock(&pool_busy);
 }

@@ -69,3 +69,35 @@ def test_no_alloc_pick_refuses_sizes_beyond_its_limit(cuda_lib, pkg):
     rc = pkg.lib().b200_argmax_f32_noalloc(int(y.data_ptr()), LIMIT + 1, 0, int(out.data_ptr()), None)
     assert rc == -22
     assert b"limit" in pkg.lib().b200_last_error()
+
+
+def _scan(y: np.ndarray) -> int:
+    """The reference's pick (tp_llama.cpp:879-882): best = 0, then i wins only if y[i] > y[best]."""
+    best = 0
+    for i in range(1, y.size):
+        if y[i] > y[best]:
+            best = i
+    return best
+
+
+@pytest.mark.parametrize("case", ["nan_at_0", "nan_inside", "small_one_cta", "single"])
+def test_no_alloc_pick_edge_inputs(cuda_lib, pkg, case):
+    """NaN at index 0 (the scan never leaves it), NaN elsewhere (never picked),
+    a vector small enough for one CTA, and n = 1: the engine's pick and the
+    reference's scan, restated."""
+    import torch
+    rng = np.random.default_rng(11)
+    n = {"nan_at_0": 5000, "nan_inside": 70000, "small_one_cta": 1000, "single": 1}[case]
+    ynp = rng.standard_normal(n).astype(np.float32)
+    if case == "nan_at_0":
+        ynp[0] = np.nan
+    if case == "nan_inside":
+        ynp[123] = np.nan
+        ynp[60000] = np.nan
+    y = torch.from_numpy(ynp).cuda()
+    eng = pkg.Engine(0)
+    want = _pick_engine(torch, pkg, eng, y, 0)
+    got = _pick_noalloc(torch, pkg, y, 0, 0)
+    eng.close()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert int(got[0]) == _scan(ynp)
