@@ -85,7 +85,7 @@ __device__ __forceinline__ uint64_t *attn_rec(uint64_t *trace) {
 }
 
 template <int D, int ESZ>
-__global__ void __maxnreg__(88) attn_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_constant__ AttnParams p) {
     constexpr int kRowBytes = D * ESZ;
     constexpr int kSegs = kRowBytes / 16;
     constexpr int kPer = 16 / ESZ;  // elements per 16 bytes
@@ -163,20 +163,14 @@ __global__ void __maxnreg__(88) attn_kernel(const __grid_constant__ AttnParams p
     if (tid < CW)
         bulk_g2s(vt + tid * S.col_stride, vtb + static_cast<size_t>(c0 + tid) * p.stride * ESZ, colb, &bars[0], pol);
 
-    // scores of positions [r0, r1) (tp_llama.cpp:652-664), to every CTA: four
-    // threads per position, thread j running fused-multiply-add lane j
-    // (elements i = j, j+4, ... in order) of every head; the lanes meet as
-    // (l0 + l1) + (l2 + l3) by xor shuffles 1 then 2 -- vaddvq_f32's pairing --
-    // so the four threads hold the same score and thread j stores it into
-    // CTA j's shared memory
+    // scores of positions [r0, r1) (tp_llama.cpp:652-664), to every CTA
     if (krows && !wait_stage(&bars[1], 0u, p.status)) atomicExch(&s_fail, 1);
-    const int jl = tid & 3;
-    for (int t0 = r0; t0 < r1; t0 += kAttnThreads / 4) {  // the same trip count in every thread
-        const int t = t0 + (tid >> 2);
-        const bool live = t < r1;
-        const uint8_t *row = kbuf + (live ? t - r0 : 0) * kRowBytes;
+    for (int t = r0 + tid; t < r1; t += kAttnThreads) {
+        const uint8_t *row = kbuf + (t - r0) * kRowBytes;
         const int sw = t & 7;
-        float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        float a[4][4];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) a[b][0] = a[b][1] = a[b][2] = a[b][3] = 0.0f;
 #pragma unroll
         for (int s8 = 0; s8 < kSegs; s8 += 8) {
             uint4 kr[8];
@@ -184,23 +178,36 @@ __global__ void __maxnreg__(88) attn_kernel(const __grid_constant__ AttnParams p
             for (int j = 0; j < 8; ++j) kr[j] = *reinterpret_cast<const uint4 *>(row + (s8 + (j ^ sw)) * 16);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                float f[kPer / 4];
-                attn_seg_lane<ESZ>(kr[j], jl, f);
+                float f[8];
+                attn_seg_floats<ESZ>(kr[j], f);
                 const int i0 = (s8 + j) * kPer;
-                // qs holds 4 heads; a head past G is computed, never used
+                // the segment's q of all four heads loaded together, then the
+                // FMAs (qs holds 4 heads; a head past G is computed, never used)
+                float4 qv[4][kPer / 4];
 #pragma unroll
                 for (int b = 0; b < 4; ++b)
 #pragma unroll
-                    for (int u = 0; u < kPer / 4; ++u) a[b] = __fmaf_rn(f[u], qs[b * D + i0 + 4 * u + jl], a[b]);
+                    for (int m4 = 0; m4 < kPer; m4 += 4) qv[b][m4 / 4] = *reinterpret_cast<const float4 *>(qs + b * D + i0 + m4);
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+#pragma unroll
+                    for (int m4 = 0; m4 < kPer; m4 += 4) {
+                        const float4 q4 = qv[b][m4 / 4];
+                        a[b][0] = __fmaf_rn(f[m4], q4.x, a[b][0]);
+                        a[b][1] = __fmaf_rn(f[m4 + 1], q4.y, a[b][1]);
+                        a[b][2] = __fmaf_rn(f[m4 + 2], q4.z, a[b][2]);
+                        a[b][3] = __fmaf_rn(f[m4 + 3], q4.w, a[b][3]);
+                    }
+                }
             }
         }
         float sv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const float x = __fadd_rn(a[b], __shfl_xor_sync(kFullMask, a[b], 1));
-            if (b < G) sv[b] = __fmul_rn(__fadd_rn(x, __shfl_xor_sync(kFullMask, x, 2)), p.scale);
-        }
-        if (live) st_cluster_f4(cluster_map(&e[t], static_cast<uint32_t>(jl)), make_float4(sv[0], sv[1], sv[2], sv[3]));
+        for (int b = 0; b < 4; ++b)
+            if (b < G) sv[b] = __fmul_rn(__fadd_rn(__fadd_rn(a[b][0], a[b][1]), __fadd_rn(a[b][2], a[b][3])), p.scale);
+        const float4 s4 = make_float4(sv[0], sv[1], sv[2], sv[3]);
+#pragma unroll
+        for (int q = 0; q < kSplit; ++q) st_cluster_f4(cluster_map(&e[t], static_cast<uint32_t>(q)), s4);
     }
     cluster_sync_all();  // every CTA now holds all n scores
     attn_stamp_at(rec, 5);
@@ -231,9 +238,6 @@ __global__ void __maxnreg__(88) attn_kernel(const __grid_constant__ AttnParams p
         m[2] = attn_max_gt(m[2], pw.z);
         m[3] = attn_max_gt(m[3], pw.w);
     }
-    // the exponentials, into e and lane-major into pv for the sums: position
-    // 4u + j of head b at pv[(4 b + j) * (stride / 4) + u]
-    const int q4 = p.stride / 4;
     for (int t = tid; t < n; t += kAttnThreads) {
         float4 s = e[t];
         s.x = v_expf(__fsub_rn(s.x, m[0]));
@@ -241,41 +245,24 @@ __global__ void __maxnreg__(88) attn_kernel(const __grid_constant__ AttnParams p
         if (G > 2) s.z = v_expf(__fsub_rn(s.z, m[2]));
         if (G > 3) s.w = v_expf(__fsub_rn(s.w, m[3]));
         e[t] = s;
-        const int j = t & 3, u = t >> 2;
-        pv[j * q4 + u] = s.x;
-        pv[(4 + j) * q4 + u] = s.y;
-        pv[(8 + j) * q4 + u] = s.z;
-        pv[(12 + j) * q4 + u] = s.w;
     }
     __syncthreads();
     attn_stamp_at(rec, 6);
 
     // sums (softmax_exp, tp_llama.cpp:626-633): warp 0, lane 4 * head + j
-    // adds positions j, j+4, ... below n - n % 4 in order, reading its row of
-    // pv 16 bytes at a time; (l0 + l1) + (l2 + l3) by two xor shuffles; then
-    // the tail one by one; inv = 1 / sum
+    // adds positions j, j+4, ... below n - n % 4 in order; (l0 + l1) + (l2 + l3)
+    // by two xor shuffles; then the tail one by one; inv = 1 / sum
     if (warp == 0) {
-        const int b = lane >> 2, j4 = lane & 3, n4 = n & ~3, nu = n4 / 4;
-        const float *lrow = pv + (4 * b + j4) * q4;
+        const int b = lane >> 2, j4 = lane & 3, n4 = n & ~3;
+        const float *col = reinterpret_cast<const float *>(e) + b;
         float acc = 0.0f;
         if (b < G) {
-            int u = 0;
-            if ((q4 & 3) == 0) {  // 16-byte rows
-#pragma unroll 4
-                for (; u + 4 <= nu; u += 4) {
-                    const float4 v4 = *reinterpret_cast<const float4 *>(lrow + u);
-                    acc = __fadd_rn(acc, v4.x);
-                    acc = __fadd_rn(acc, v4.y);
-                    acc = __fadd_rn(acc, v4.z);
-                    acc = __fadd_rn(acc, v4.w);
-                }
-            }
-            for (; u < nu; ++u) acc = __fadd_rn(acc, lrow[u]);
+#pragma unroll 16
+            for (int t = j4; t < n4; t += 4) acc = __fadd_rn(acc, col[4 * t]);
         }
         const float x = __fadd_rn(acc, __shfl_xor_sync(kFullMask, acc, 1));
         const float y = __fadd_rn(x, __shfl_xor_sync(kFullMask, x, 2));
         if (b < G && j4 == 0) {
-            const float *col = reinterpret_cast<const float *>(e) + b;
             float sum = y;
             for (int t = n4; t < n; ++t) sum = __fadd_rn(sum, col[4 * t]);
             hinv[b] = __frcp_rn(sum);  // IEEE 1 / sum, round to nearest: the reference's 1.0f / sum
