@@ -98,7 +98,8 @@ struct b200_decoder {
     void *sel_scratch;
     uint8_t *kv;
     bool output_set;
-    cudaGraphExec_t graph;
+    cudaGraphExec_t graph;   // one token
+    cudaGraphExec_t graphk;  // kGraphTokens tokens in a row: dependent launches overlap across token boundaries too
     int host_pos;       // where the device loop stands after the work queued so far
     int32_t *host_io;   // pinned, mapped: [0, 2) the pick, [2, 2 + ctx_max + 1) token ids by position
     Tuning tu;
@@ -442,6 +443,36 @@ int build_phases(b200_decoder_t *d) {
     return 0;
 }
 
+constexpr int kGraphTokens = 8;
+
+// Capture `tokens` tokens' launches into an executable graph.
+int capture_tokens(b200_decoder_t *d, int tokens, cudaGraphExec_t *out) {
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeRelaxed);
+    if (e != cudaSuccess) return dfail(kErrCuda, "decoder: capture begin failed: %s", cudaGetErrorString(e));
+    int rc = 0;
+    for (int t = 0; t < tokens && !rc; ++t) rc = enqueue_token(d);
+    e = cudaStreamEndCapture(d->stream, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return dfail(kErrCuda, "decoder: capture failed: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+        *out = nullptr;
+        return dfail(kErrCuda, "decoder: graph instantiation failed: %s", cudaGetErrorString(e));
+    }
+    return 0;
+}
+
+void drop_graphs(b200_decoder_t *d) {
+    if (d->graph) cudaGraphExecDestroy(d->graph);
+    if (d->graphk) cudaGraphExecDestroy(d->graphk);
+    d->graph = d->graphk = nullptr;
+}
+
 int ready(b200_decoder_t *d) {
     if (!d) return dfail(kErrInval, "decoder: null handle");
     for (const DecLayer &L : d->layers)
@@ -449,22 +480,12 @@ int ready(b200_decoder_t *d) {
     if (!d->output_set) return dfail(kErrInval, "decoder: token_embd / output_norm not set");
     if (int rc = use_dev(d)) return rc;
     if (d->persistent) return d->nphases ? 0 : build_phases(d);
-    if (d->graph) return 0;
-    cudaGraph_t g = nullptr;
-    cudaError_t e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeRelaxed);
-    if (e != cudaSuccess) return dfail(kErrCuda, "decoder: capture begin failed: %s", cudaGetErrorString(e));
-    const int rc = enqueue_token(d);
-    e = cudaStreamEndCapture(d->stream, &g);
-    if (rc) {
-        if (g) cudaGraphDestroy(g);
+    if (d->graph && d->graphk) return 0;
+    drop_graphs(d);
+    if (int rc = capture_tokens(d, 1, &d->graph)) return rc;
+    if (int rc = capture_tokens(d, kGraphTokens, &d->graphk)) {
+        drop_graphs(d);
         return rc;
-    }
-    if (e != cudaSuccess) return dfail(kErrCuda, "decoder: capture failed: %s", cudaGetErrorString(e));
-    e = cudaGraphInstantiate(&d->graph, g, 0);
-    cudaGraphDestroy(g);
-    if (e != cudaSuccess) {
-        d->graph = nullptr;
-        return dfail(kErrCuda, "decoder: graph instantiation failed: %s", cudaGetErrorString(e));
     }
     return 0;
 }
@@ -488,9 +509,12 @@ int launch_steps(b200_decoder_t *d, int n) {
         d->host_pos += n;
         return 0;
     }
-    for (int i = 0; i < n; ++i)
-        if (cudaGraphLaunch(d->graph, d->stream) != cudaSuccess)
+    for (int i = 0; i < n;) {
+        const bool k = n - i >= kGraphTokens;
+        if (cudaGraphLaunch(k ? d->graphk : d->graph, d->stream) != cudaSuccess)
             return dfail(kErrCuda, "decoder: graph launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+        i += k ? kGraphTokens : 1;
+    }
     d->host_pos += n;
     return 0;
 }
@@ -801,10 +825,7 @@ extern "C" int b200_decoder_trace(b200_decoder_t *d, int tokens) {
             if (cudaMemset(d->trace, 0, bytes) != cudaSuccess) return dfail(kErrCuda, "decoder: trace reset failed");
             d->trace_launches = nl;
         }
-        if (tokens != d->trace_tokens && d->graph) {  // recapture with (or without) the trace pointers
-            cudaGraphExecDestroy(d->graph);
-            d->graph = nullptr;
-        }
+        if (tokens != d->trace_tokens) drop_graphs(d);  // recapture with (or without) the trace pointers
         d->trace_tokens = tokens;
         if (!tokens) {
             d->trace = nullptr;
@@ -909,7 +930,7 @@ extern "C" int b200_decoder_destroy(b200_decoder_t *d) {
     cudaGetDevice(&cur);
     if (cur != d->device) cudaSetDevice(d->device);
     if (d->stream) cudaStreamSynchronize(d->stream);
-    if (d->graph) cudaGraphExecDestroy(d->graph);
+    drop_graphs(d);
     for (void *p : d->allocs) cudaFree(p);
     if (d->host_io) cudaFreeHost(d->host_io);
     if (d->stream) cudaStreamDestroy(d->stream);
