@@ -396,21 +396,37 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         l2_resident = {"value": 1e3 / l2_ms, "unit": UNIT, "ms_per_step": l2_ms,
                        "how": "the same positions, no flush: the rank's weights stay in L2 across tokens"}
 
-    # End to end through the public call (b200_decoder_generate): host prompt
-    # in, every token copied to host memory as it is made, host wall clock
-    # around the call. The decode phase is the difference between a call that
-    # generates steps + 1 tokens and one that generates only the prompt's pick.
+    # End to end through the public per-token call, as the reference runtime's
+    # generate drives forward (tp_llama.cpp:942-968): every step the host
+    # hands the token and position in from pinned memory and reads the pick
+    # (and the status words) back, b200_decoder_forward waiting once; host
+    # wall clock around the K steps, max over ranks. The prompt is prefilled
+    # untimed.
+    barrier(world)
+    dec.prefill(prompt)
+    torch.cuda.synchronize()
+    tok = int(dec.tokens()[n_prompt])
+    pos = n_prompt
+    e2e_tokens = [tok]
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok, _ = dec.forward(tok, pos)
+        e2e_tokens.append(tok)
+        pos += 1
+    wall = max_over_ranks(time.perf_counter() - t0, world)
+    e2e_same = bool(np.array_equal(np.asarray(e2e_tokens, np.int32), timed_tokens[:args.steps + 1]))
+    # the queued loop through b200_decoder_generate (host prompt in, each token
+    # copied out as it is made, one wait): the difference of a call making
+    # steps + 1 tokens and one making only the prompt's pick
     walls = []
     for n_gen in (1, args.steps + 1):
         barrier(world)
         torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        e2e_tokens, _, gen_ms = dec.generate(prompt, n_gen)
-        walls.append(time.perf_counter() - t0)
-    wall_1 = max_over_ranks(walls[0], world)
-    wall_n = max_over_ranks(walls[1], world)
-    gen_ms = max_over_ranks(gen_ms, world)
-    e2e_same = bool(np.array_equal(e2e_tokens, timed_tokens[:args.steps + 1]))
+        t1 = time.perf_counter()
+        dec.generate(prompt, n_gen)
+        walls.append(time.perf_counter() - t1)
+    gen_wall = max_over_ranks(walls[1], world) - max_over_ranks(walls[0], world)
 
     per_gemv = per_gemv_table(pkg, torch, world, local_rank) if args.per_gemv else None
     peak, peak_kind = hbm_peak()
@@ -467,14 +483,15 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
             "cpu_baseline": cpu,
             "token_check": check,
             "l2_resident": l2_resident,
-            "e2e": {"value": args.steps / (wall_n - wall_1), "unit": UNIT, "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 4, "h2d_bytes_per_call": 4 * n_prompt,
-                    "call": "b200_decoder_generate: host prompt in, each token copied to host memory as it is "
-                            "made; host wall clock around the call (max over ranks)",
-                    "method": f"{args.steps} decode tokens / (wall of a call making {args.steps + 1} tokens - "
-                              "wall of a call making the prompt's pick only)",
-                    "wall_s": [wall_1, wall_n], "device_ms_generation": gen_ms,
-                    "tokens_same_as_timed_run": e2e_same},
+            "e2e": {"value": args.steps / wall, "unit": UNIT, "h2d_bytes_per_step": 12,
+                    "d2h_bytes_per_step": 8 + 4 + (4 if world > 1 else 0),
+                    "call": "b200_decoder_forward per token: token, position and prompt length in from pinned host "
+                            "memory (12 B), the pick (8 B) and the status words back, one wait per token; host wall "
+                            "clock around the steps (max over ranks)",
+                    "tokens_same_as_timed_run": e2e_same,
+                    "generate_call": {"value": args.steps / gen_wall, "unit": UNIT,
+                                      "call": "b200_decoder_generate: the same loop queued, each token copied to "
+                                              "host memory as it is made, one wait per call"}},
             "gpu_launches": launches,
             "clocks": clocks,
             "status": status,

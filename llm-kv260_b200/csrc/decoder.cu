@@ -24,6 +24,7 @@
 #include <cuda_runtime.h>
 
 #include <climits>
+#include <cstddef>
 #include <cstdarg>
 #include <cmath>
 #include <cstdio>
@@ -52,8 +53,8 @@ struct DecLayer {
 // small device state, one allocation
 struct DevState {
     int pos;
+    int n_prompt;       // next to pos: forward() sets both with one copy
     unsigned step;
-    int n_prompt;
     int pad;
     int pick[2];        // the token (int32) and its logit (float32 bits)
     int pick_local[2];  // several ranks: this rank's pick over its vocab shard
@@ -80,6 +81,10 @@ int dfail(int code, const char *fmt, ...) {
 
 }  // namespace
 
+namespace {
+constexpr int kIoSlots = 5;  // forward(): token, position, n_prompt, then the status and peer status words
+}  // namespace
+
 struct b200_decoder {
     b200_decoder_config_t c;
     int device, rank, nranks;
@@ -101,7 +106,8 @@ struct b200_decoder {
     cudaGraphExec_t graph;   // one token
     cudaGraphExec_t graphk;  // kGraphTokens tokens in a row: dependent launches overlap across token boundaries too
     int host_pos;       // where the device loop stands after the work queued so far
-    int32_t *host_io;   // pinned, mapped: [0, 2) the pick, [2, 2 + ctx_max + 1) token ids by position
+    int32_t *host_io;   // pinned, mapped: [0, 2) the pick, [2, 2 + ctx_max + 1) token ids by position, then
+                        // kIoSlots words for forward(): token, position, n_prompt in; status words out
     Tuning tu;
     // persistent mode
     bool persistent;
@@ -620,7 +626,7 @@ extern "C" int b200_decoder_create(b200_decoder_t **out, const b200_decoder_conf
     if (!rc) rc = dalloc(d, &d->kv, 2 * kv_bytes);
     if (!rc) rc = dalloc(d, &d->output_norm, 4 * static_cast<size_t>(e));
     if (rc) return bail(rc);
-    if (cudaHostAlloc(reinterpret_cast<void **>(&d->host_io), 4 * (static_cast<size_t>(c.ctx_max) + 3),
+    if (cudaHostAlloc(reinterpret_cast<void **>(&d->host_io), 4 * (static_cast<size_t>(c.ctx_max) + 3 + kIoSlots),
                       cudaHostAllocMapped) != cudaSuccess)
         return bail(dfail(kErrNoMem, "decoder: pinned host buffer allocation failed"));
     d->persistent = c.persistent != 0;
@@ -747,13 +753,30 @@ extern "C" int b200_decoder_forward(b200_decoder_t *d, int token, int pos, int32
     if (int rc = ready(d)) return rc;
     if (token < 0 || token >= d->c.n_vocab || pos < 0 || pos >= d->c.ctx_max)
         return dfail(kErrInval, "decoder: token or position out of range");
-    if (int rc = h2d(d->tokens + pos, &token, 4, d->stream)) return rc;
-    if (int rc = set_state(d, pos, INT_MAX)) return rc;  // the loop's advance writes no token
-    if (int rc = launch_steps(d, 1)) return rc;
-    cudaMemcpyAsync(d->host_io, d->st->pick, 8, cudaMemcpyDeviceToHost, d->stream);
+    // The step's inputs go from pinned host memory, its result and the status
+    // words come back into it, and the call waits once. Earlier queued work
+    // (prefill / step) finishes first, so the pinned words are free.
     if (cudaStreamSynchronize(d->stream) != cudaSuccess)
-        return dfail(kErrCuda, "decoder: forward failed: %s", cudaGetErrorString(cudaGetLastError()));
-    if (int rc = check_status(d)) return rc;
+        return dfail(kErrCuda, "decoder: stream failed: %s", cudaGetErrorString(cudaGetLastError()));
+    int32_t *io = d->host_io + 3 + d->c.ctx_max;  // kIoSlots words
+    io[0] = token;
+    io[1] = pos;
+    io[2] = INT_MAX;  // n_prompt: the loop's advance writes no token
+    io[3] = io[4] = 0;
+    static_assert(offsetof(DevState, n_prompt) == offsetof(DevState, pos) + 4, "pos and n_prompt adjacent");
+    cudaError_t e = cudaMemcpyAsync(d->tokens + pos, io, 4, cudaMemcpyHostToDevice, d->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&d->st->pos, io + 1, 8, cudaMemcpyHostToDevice, d->stream);
+    if (e != cudaSuccess) return dfail(kErrCuda, "decoder: copy to the device failed: %s", cudaGetErrorString(e));
+    d->host_pos = pos;
+    if (int rc = launch_steps(d, 1)) return rc;
+    e = cudaMemcpyAsync(d->host_io, d->st->pick, 8, cudaMemcpyDeviceToHost, d->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(io + 3, status_word(), 4, cudaMemcpyDeviceToHost, d->stream);
+    if (e == cudaSuccess && d->peer_status) e = cudaMemcpyAsync(io + 4, d->peer_status, 4, cudaMemcpyDeviceToHost, d->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+    if (e != cudaSuccess) return dfail(kErrCuda, "decoder: forward failed: %s", cudaGetErrorString(e));
+    if (io[3] || io[4] || d->persistent) {
+        if (int rc = check_status(d)) return rc;  // the full check (and the persistent kernel's abort flag)
+    }
     if (pick) *pick = d->host_io[0];
     if (value) memcpy(value, &d->host_io[1], 4);
     return 0;
