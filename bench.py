@@ -301,6 +301,23 @@ def per_gemv_table(pkg, torch, world: int, device: int, launches: int = 200) -> 
     return out
 
 
+def launch_floor(pkg, device: int, launches: int, reps: int = 200) -> dict:
+    """What the token's launch chain costs with nothing in it: `launches`
+    empty kernels of the GEMVs' shape (148 CTAs x 288 threads) in one CUDA
+    graph, with programmatic dependent launch as the decoder uses it, with a
+    200 KB shared-memory request (one CTA per SM, so a kernel's CTAs cannot
+    start beside its predecessor's), and in plain stream order; microseconds
+    per launch from CUDA events around `reps` replays."""
+    import ctypes
+    lib = pkg.capi.lib()
+    out = {"launches": launches, "ctas": 148, "threads": 288}
+    for key, smem, pdl in (("pdl_us", 0, 1), ("pdl_smem200k_us", 200 * 1024, 1), ("plain_us", 0, 0)):
+        us = ctypes.c_float(0.0)
+        rc = lib.b200_launch_floor(device, launches, 148, 288, smem, pdl, reps, ctypes.byref(us))
+        out[key] = round(us.value, 3) if rc == 0 else None
+    return out
+
+
 def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     import torch
     import __graft_entry__
@@ -429,6 +446,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     gen_wall = max_over_ranks(walls[1], world) - max_over_ranks(walls[0], world)
 
     per_gemv = per_gemv_table(pkg, torch, world, local_rank) if args.per_gemv else None
+    floor = None if persistent else launch_floor(pkg, local_rank, 5 * hp["n_layer"] + 1 + (2 if world > 1 else 0))
     peak, peak_kind = hbm_peak()
     achieved = gemv_bytes / (ms_per_step * 1e-3) / 1e9
 
@@ -493,6 +511,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                                       "call": "b200_decoder_generate: the same loop queued, each token copied to "
                                               "host memory as it is made, one wait per call"}},
             "gpu_launches": launches,
+            "launch_floor": floor,
             "clocks": clocks,
             "status": status,
         }

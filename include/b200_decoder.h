@@ -142,6 +142,18 @@ B200_API int b200_decoder_set_rope_freqs(b200_decoder_t *d, const float *freqs);
 B200_API int b200_rope_table(float *cs, int d, int pos, float base);
 B200_API int b200_rope_table_freqs(float *cs, int d, int pos, float base, const float *freqs);
 
+/* The cost of the decoder's launch chain alone: `launches` empty kernels of
+ * `ctas` CTAs x `threads` threads, each asking for `smem` bytes of dynamic
+ * shared memory, captured into one CUDA graph on device `device` -- with
+ * programmatic dependent launch when `pdl` is nonzero (each kernel lets its
+ * dependents launch at once, then waits for its predecessor, as the
+ * decoder's kernels do), else plain stream order -- replayed `reps` times
+ * after three untimed replays and timed with CUDA events. *us_per_launch =
+ * the mean time per launch in microseconds. A B200 diagnostic with no
+ * reference counterpart. */
+B200_API int b200_launch_floor(int device, int launches, int ctas, int threads, int smem, int pdl, int reps,
+                               float *us_per_launch);
+
 /* The decoder's CUDA stream (cudaStream_t). */
 B200_API void *b200_decoder_stream(b200_decoder_t *d);
 

@@ -128,6 +128,7 @@ SIGNATURES: dict[str, tuple] = {
     "b200_decoder_read": (c_int, [c_vp, c_int, c_vp, c_u64]),
     "b200_decoder_status": (c_int, [c_vp, P(c_uint)]),
     "b200_decoder_trace": (c_int, [c_vp, c_int]),
+    "b200_launch_floor": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, P(ctypes.c_float)]),
     "b200_rope_table": (c_int, [c_vp, c_int, c_int, ctypes.c_float]),
     "b200_rope_table_freqs": (c_int, [c_vp, c_int, c_int, ctypes.c_float, c_vp]),
     "b200_decoder_set_rope_freqs": (c_int, [c_vp, c_vp]),

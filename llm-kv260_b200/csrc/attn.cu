@@ -6,10 +6,11 @@
 // One thread-block cluster of kSplit CTAs per local KV head. CTA r of the
 // cluster:
 //   scores  the positions [r * per, (r + 1) * per) (per = ceil(n / kSplit)):
-//           its K rows land in shared memory by one bulk copy (rows swizzled
-//           by position, k_swizzled), one thread per position as attn_core
-//           does, and every score row (4 heads) goes to every CTA of the
-//           cluster through distributed shared memory; one cluster barrier;
+//           its K rows land in shared memory by one bulk copy (lane-major
+//           rows, k_slot), one thread per position runs the four FMA lanes
+//           of every head (q lane-major in shared memory too), and every
+//           score row (4 heads) goes to every CTA of the cluster through
+//           distributed shared memory; one cluster barrier;
 //   softmax every CTA then holds all n scores and runs the reference's max,
 //           v_expf, four-lane sums and 1 / sum itself -- the same operations
 //           in the same order on the same values, so the same bits;
@@ -90,6 +91,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
     constexpr int kSegs = kRowBytes / 16;
     constexpr int kPer = 16 / ESZ;  // elements per 16 bytes
     constexpr int CW = D / kSplit;  // output columns per CTA
+    constexpr int L = kSegs / 4, M = D / 4;  // per FMA lane: K segments, steps
     constexpr int kQv = (4 * D + kAttnThreads - 1) / kAttnThreads;
     static_assert(kSegs % 8 == 0 && kPer % 4 == 0 && 4 * CW <= kAttnThreads, "attention shape");
     extern __shared__ __align__(128) uint8_t smem[];
@@ -97,7 +99,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
     __shared__ int s_fail;
     const AttnSmem S = attn_smem_layout(D, ESZ, p.stride);
     uint8_t *kbuf = smem + S.kbuf, *vt = smem + S.vt;
-    float *qs = reinterpret_cast<float *>(smem + S.qs);
+    float *qs = reinterpret_cast<float *>(smem + S.qs);  // [head][lane j][step m]: element 4m + j
     float *part = reinterpret_cast<float *>(smem + S.part);
     float *hinv = reinterpret_cast<float *>(smem + S.hinv);
     float4 *e = reinterpret_cast<float4 *>(smem + S.e);  // [position]: the 4 heads' scores, then exponentials
@@ -152,7 +154,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
 #pragma unroll
     for (int u = 0; u < kQv; ++u) {
         const int i = tid + u * kAttnThreads;
-        if (i < G * D) qs[i] = qv[u];
+        if (i < G * D) qs[(i / D) * D + (i & 3) * M + (i % D) / 4] = qv[u];
     }
     __syncthreads();
     attn_stamp_at(rec, 4);
@@ -173,30 +175,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
         for (int b = 0; b < 4; ++b) a[b][0] = a[b][1] = a[b][2] = a[b][3] = 0.0f;
 #pragma unroll
         for (int s8 = 0; s8 < kSegs; s8 += 8) {
+            // logical segments s8 .. s8 + 7, loaded in an order that puts the
+            // lanes (8 consecutive positions) on distinct bank groups
+            const int g = 2 * ((s8 >> 3) & 3);
             uint4 kr[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) kr[j] = *reinterpret_cast<const uint4 *>(row + (s8 + (j ^ sw)) * 16);
+            for (int j = 0; j < 8; ++j) kr[j] = *reinterpret_cast<const uint4 *>(row + (s8 + (j ^ sw ^ g)) * 16);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
+                // logical segment s: FMA lane s / L, steps (s % L) * kPer ..
+                const int sg = s8 + j, ln = sg / L, m0 = (sg % L) * kPer;
                 float f[8];
                 attn_seg_floats<ESZ>(kr[j], f);
-                const int i0 = (s8 + j) * kPer;
                 // the segment's q of all four heads loaded together, then the
                 // FMAs (qs holds 4 heads; a head past G is computed, never used)
-                float4 qv[4][kPer / 4];
+                float4 qv4[4][kPer / 4];
 #pragma unroll
                 for (int b = 0; b < 4; ++b)
 #pragma unroll
-                    for (int m4 = 0; m4 < kPer; m4 += 4) qv[b][m4 / 4] = *reinterpret_cast<const float4 *>(qs + b * D + i0 + m4);
+                    for (int m4 = 0; m4 < kPer; m4 += 4)
+                        qv4[b][m4 / 4] = *reinterpret_cast<const float4 *>(qs + b * D + ln * M + m0 + m4);
 #pragma unroll
                 for (int b = 0; b < 4; ++b) {
 #pragma unroll
-                    for (int m4 = 0; m4 < kPer; m4 += 4) {
-                        const float4 q4 = qv[b][m4 / 4];
-                        a[b][0] = __fmaf_rn(f[m4], q4.x, a[b][0]);
-                        a[b][1] = __fmaf_rn(f[m4 + 1], q4.y, a[b][1]);
-                        a[b][2] = __fmaf_rn(f[m4 + 2], q4.z, a[b][2]);
-                        a[b][3] = __fmaf_rn(f[m4 + 3], q4.w, a[b][3]);
+                    for (int u = 0; u < kPer; ++u) {
+                        const float4 q4 = qv4[b][u / 4];
+                        const float qu = (u & 3) == 0 ? q4.x : (u & 3) == 1 ? q4.y : (u & 3) == 2 ? q4.z : q4.w;
+                        a[b][ln] = __fmaf_rn(f[u], qu, a[b][ln]);
                     }
                 }
             }
@@ -330,9 +335,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
 // Long contexts, cluster form: the cluster kernel's split (CTA r scores a
 // quarter of the positions and chains a quarter of the columns) with K and
 // V^T streamed through rings of shared-memory stages instead of held whole.
-//   scores  4 threads per position (fused-multiply-add lane j each, met by
-//           xor shuffles 1 then 2: vaddvq_f32's pairing); every score row to
-//           all four CTAs (distributed shared memory); one cluster barrier;
+//   scores  4 threads per position (fused-multiply-add lane j each: q's
+//           elements j, j+4, ... of every head in registers, the lane's
+//           quarter of the lane-major K row from the ring; met by xor
+//           shuffles 1 then 2: vaddvq_f32's pairing); every score row to all
+//           four CTAs (distributed shared memory); one cluster barrier;
 //   softmax each CTA: maxima, v_expf, the four sequential lane sums per head
 //           read from a lane-major copy of the exponentials, 1 / sum, p;
 //   output  one thread per (column, head): the fused-multiply-add chain over
@@ -455,8 +462,17 @@ __global__ void __launch_bounds__(kStreamThreads, 1) attn_stream_kernel(const __
     __syncthreads();
     attn_stamp_at(rec, 4);
 
-    // scores of positions [r0, r1) (tp_llama.cpp:652-664), to every CTA
+    // scores of positions [r0, r1) (tp_llama.cpp:652-664), to every CTA:
+    // four threads per position, thread jl running FMA lane jl of every
+    // head -- its q elements jl, jl+4, ... held in registers, its quarter of
+    // the lane-major K row (k_slot) read as L 16-byte segments
     const int jl = tid & 3;
+    constexpr int L = kSegs / 4, M = D / 4;
+    float qr[4][M];
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+#pragma unroll
+        for (int m = 0; m < M; ++m) qr[b][m] = b < G ? qs[b * D + 4 * m + jl] : 0.0f;
     for (int kc = 0; kc < nk; ++kc) {
         const int a0 = r0 + kc * KC, a1 = min(r1, a0 + KC), st = kc % kStreamKStages;
         if (!s_fail && !wait_stage(&kbar[st], static_cast<uint32_t>((kc / kStreamKStages) & 1), p.status))
@@ -466,25 +482,19 @@ __global__ void __launch_bounds__(kStreamThreads, 1) attn_stream_kernel(const __
             const int t = t0 + (tid >> 2);
             const bool live = t < a1;
             const uint8_t *row = kst + (live ? t - a0 : 0) * kRowBytes;
-            const int sw = t & 7;
             float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            uint4 kr[L];
 #pragma unroll
-            for (int s8 = 0; s8 < kSegs; s8 += 8) {
-                uint4 kr[8];
+            for (int i = 0; i < L; ++i) kr[i] = *reinterpret_cast<const uint4 *>(row + k_phys_seg(jl * L + i, t) * 16);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) kr[j] = *reinterpret_cast<const uint4 *>(row + (s8 + (j ^ sw)) * 16);
+            for (int i = 0; i < L; ++i) {
+                float f[kPer];
+                attn_seg_floats<ESZ>(kr[i], f);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    float f[kPer / 4];
-                    attn_seg_lane<ESZ>(kr[j], jl, f);
-                    const int i0 = (s8 + j) * kPer;
+                for (int b = 0; b < 4; ++b) {
+                    if (b < G) {
 #pragma unroll
-                    for (int b = 0; b < 4; ++b) {
-                        if (b < G) {
-#pragma unroll
-                            for (int u = 0; u < kPer / 4; ++u)
-                                acc[b] = __fmaf_rn(f[u], qs[b * D + i0 + 4 * u + jl], acc[b]);
-                        }
+                        for (int u = 0; u < kPer; ++u) acc[b] = __fmaf_rn(f[u], qr[b][i * kPer + u], acc[b]);
                     }
                 }
             }

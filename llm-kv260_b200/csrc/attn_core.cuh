@@ -5,11 +5,14 @@
 // attention phase (token.cu).
 //
 // Cache layouts, per layer and KV head, `stride` positions per head:
-//   K   [kv head][stride][D]   a position's row contiguous, its 16-byte
-//                              segments XOR-swizzled by the position
-//                              (k_swizzled, decode.cuh): one thread reads a
-//                              whole row for its scores, and 8 consecutive
-//                              rows' segment s sit in 8 different bank groups
+//   K   [kv head][stride][D]   a position's row contiguous, lane-major
+//                              (k_slot, decode.cuh): the elements that
+//                              fused-multiply-add lane j takes (j, j+4, ...)
+//                              stored together, so the thread running lane j
+//                              reads only its quarter of the row; 16-byte
+//                              segments swizzled by the position, so the
+//                              lanes of consecutive positions read distinct
+//                              bank groups
 //   V^T [kv head][D][stride]   a column's positions contiguous: one 16-byte
 //                              shared load feeds 16 / esz steps of a chain
 // The reference keeps V position-major and K rows in order; the values and
@@ -19,9 +22,10 @@
 // bytes per column (one copy per column).
 //
 // Phases, NT threads, each in the reference's arithmetic order:
-//   scores  thread per position t: its K row from shared memory, per head
-//           four FMA lanes (element i feeds lane i & 3, i increasing), then
-//           (a0 + a1) + (a2 + a3), times scale (652-664);
+//   scores  four threads per position t, thread j running FMA lane j
+//           (element i feeds lane i & 3, i increasing) of every head from
+//           its quarter of the K row, then (a0 + a1) + (a2 + a3) by xor
+//           shuffles, times scale (652-664);
 //   max     per head, the running `>` max from -1e30f: max is exact, so a
 //           tree over threads gives the same value (no NaN ever wins, and
 //           +-0 ties give the same exponentials);
@@ -78,22 +82,6 @@ __device__ __forceinline__ void attn_seg_floats(const uint4 &v, float *f) {
         f[1] = __uint_as_float(v.y);
         f[2] = __uint_as_float(v.z);
         f[3] = __uint_as_float(v.w);
-    }
-}
-
-// The elements of 16 bytes of a K row that fused-multiply-add lane j
-// (0..3) takes: j and j + 4 (ESZ 2), or j (ESZ 4). Selected with j at run
-// time without indexing a register array.
-template <int ESZ>
-__device__ __forceinline__ void attn_seg_lane(const uint4 &v, int j, float *f) {
-    if constexpr (ESZ == 2) {
-        const bool hi = j & 2, odd = j & 1;
-        const uint32_t w0 = hi ? v.y : v.x, w1 = hi ? v.w : v.z;
-        f[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(odd ? w0 >> 16 : w0 & 0xffffu)));
-        f[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(odd ? w1 >> 16 : w1 & 0xffffu)));
-    } else {
-        const uint32_t w = (j & 2) ? ((j & 1) ? v.w : v.z) : ((j & 1) ? v.y : v.x);
-        f[0] = __uint_as_float(w);
     }
 }
 
@@ -251,25 +239,21 @@ __device__ bool attn_core(const float *q, const uint8_t *kb, const uint8_t *vtb,
             const int t = t0 + (tid >> 2);
             const bool live = t < r1;
             const uint8_t *row = kst + (live ? t - r0 : 0) * kRowBytes;
-            const int sw = t & 7;
+            // lane jl's segments jl * L .. jl * L + L - 1: steps m in order
+            constexpr int L = kSegs / 4;
             float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            uint4 kr[L];
 #pragma unroll
-            for (int s8 = 0; s8 < kSegs; s8 += 8) {
-                uint4 kr[8];
+            for (int i = 0; i < L; ++i) kr[i] = *reinterpret_cast<const uint4 *>(row + k_phys_seg(jl * L + i, t) * 16);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) kr[j] = *reinterpret_cast<const uint4 *>(row + (s8 + (j ^ sw)) * 16);
+            for (int i = 0; i < L; ++i) {
+                float f[kPer];
+                attn_seg_floats<ESZ>(kr[i], f);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    float f[kPer / 4];
-                    attn_seg_lane<ESZ>(kr[j], jl, f);
-                    const int i0 = (s8 + j) * kPer;
+                for (int b = 0; b < 4; ++b) {
+                    if (b < G) {
 #pragma unroll
-                    for (int b = 0; b < 4; ++b) {
-                        if (b < G) {
-#pragma unroll
-                            for (int u = 0; u < kPer / 4; ++u)
-                                a[b] = __fmaf_rn(f[u], qs[b * D + i0 + 4 * u + jl], a[b]);
-                        }
+                        for (int u = 0; u < kPer; ++u) a[b] = __fmaf_rn(f[u], qs[b * D + 4 * (i * kPer + u) + jl], a[b]);
                     }
                 }
             }

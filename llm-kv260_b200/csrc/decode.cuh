@@ -49,13 +49,22 @@ __device__ __forceinline__ float rope_pair(float x0, float x1, float c, float s,
 }
 
 // Where element e (0 <= e < hd) of the K row of position `pos` sits inside
-// that row in the K cache: the row's 16-byte segments are XOR-swizzled by
-// the position (segment s stored at (s & ~7) | ((s & 7) ^ (pos & 7))), so the
-// attention's threads, one row each, read 8 consecutive rows' segment s from
-// 8 different shared-memory bank groups. esz: 2 (float16) or 4 (float32).
-__host__ __device__ __forceinline__ int k_swizzled(int e, int pos, int esz) {
-    const int per = 16 / esz, s = e / per;
-    return ((s & ~7) | ((s & 7) ^ (pos & 7))) * per + e % per;
+// that row in the K cache (element index; esz 2: float16, 4: float32).
+// Lane-major: the reference's scores run four fused-multiply-add lanes, lane
+// j taking elements j, j+4, j+8, ... in order (tp_llama.cpp:652-660), so
+// element e = 4m + j is step m of lane j, and lane j's steps are stored
+// together: logical 16-byte segment s = j * L + m / (16 / esz) (L = hd * esz
+// / 64 segments per lane). Logical segment s sits at physical segment
+// (s & ~7) | ((s & 7) ^ (pos & 7) ^ 2 ((s >> 3) & 3)): the four lanes of one
+// position, the eight lanes of two consecutive positions, and one segment of
+// eight consecutive positions each fall on distinct shared-memory bank
+// groups (rows are multiples of 128 bytes).
+__host__ __device__ __forceinline__ int k_phys_seg(int s, int pos) {
+    return (s & ~7) | ((s & 7) ^ (pos & 7) ^ (2 * ((s >> 3) & 3)));
+}
+__host__ __device__ __forceinline__ int k_slot(int e, int pos, int esz, int hd) {
+    const int per = 16 / esz, lanes_segs = hd * esz / 64, j = e & 3, m = e >> 2;
+    return k_phys_seg(j * lanes_segs + m / per, pos) * per + m % per;
 }
 
 // RMSNorm's sum of squares, tp_llama.cpp:557-564: the reference sums

@@ -945,6 +945,73 @@ int decoder_config(const b200_decoder_t *d, b200_decoder_config_t *out) {
 }
 }  // namespace b200
 
+namespace {
+// An empty kernel shaped like the decoder's: it lets its dependents launch,
+// then waits for its predecessor (both no-ops without the PDL attribute).
+__global__ void launch_floor_kernel() {
+    pdl_launch_dependents();
+    pdl_wait_prior_grid();
+}
+}  // namespace
+
+extern "C" int b200_launch_floor(int device, int launches, int ctas, int threads, int smem, int pdl, int reps,
+                                 float *us_per_launch) {
+    if (!us_per_launch || launches < 1 || launches > 4096 || ctas < 1 || ctas > 65535 || threads < 32 ||
+        threads > 1024 || smem < 0 || reps < 1 || reps > 100000)
+        return dfail(kErrInval, "launch floor: bad arguments");
+    if (cudaSetDevice(device) != cudaSuccess) return dfail(kErrNoDev, "launch floor: no device %d", device);
+    if (smem > max_smem_optin()) return dfail(kErrInval, "launch floor: %d bytes of shared memory is above the limit", smem);
+    if (!ensure_smem(reinterpret_cast<const void *>(launch_floor_kernel), smem > 0 ? smem : 1))
+        return dfail(kErrCuda, "launch floor: kernel attributes");
+    cudaStream_t st = nullptr;
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    int rc = 0;
+    auto fail = [&](const char *what) {
+        rc = dfail(kErrCuda, "launch floor: %s: %s", what, cudaGetErrorString(cudaGetLastError()));
+    };
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) {
+        fail("stream");
+    } else if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        fail("capture");
+    } else {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(static_cast<unsigned>(ctas));
+        cfg.blockDim = dim3(static_cast<unsigned>(threads));
+        cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = pdl ? 1 : 0;
+        bool ok = true;
+        for (int i = 0; i < launches && ok; ++i) ok = cudaLaunchKernelEx(&cfg, launch_floor_kernel) == cudaSuccess;
+        const bool ended = cudaStreamEndCapture(st, &g) == cudaSuccess;
+        if (!ok || !ended) fail("launch");
+        else if (cudaGraphInstantiate(&ge, g, 0) != cudaSuccess) fail("instantiate");
+    }
+    if (!rc) {
+        bool ok = cudaEventCreate(&e0) == cudaSuccess && cudaEventCreate(&e1) == cudaSuccess;
+        for (int i = 0; i < 3 && ok; ++i) ok = cudaGraphLaunch(ge, st) == cudaSuccess;
+        ok = ok && cudaEventRecord(e0, st) == cudaSuccess;
+        for (int i = 0; i < reps && ok; ++i) ok = cudaGraphLaunch(ge, st) == cudaSuccess;
+        ok = ok && cudaEventRecord(e1, st) == cudaSuccess && cudaEventSynchronize(e1) == cudaSuccess;
+        float ms = 0.0f;
+        ok = ok && cudaEventElapsedTime(&ms, e0, e1) == cudaSuccess;
+        if (!ok) fail("replay");
+        else *us_per_launch = 1e3f * ms / (static_cast<float>(reps) * static_cast<float>(launches));
+    }
+    if (st) cudaStreamSynchronize(st);
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (ge) cudaGraphExecDestroy(ge);
+    if (g) cudaGraphDestroy(g);
+    if (st) cudaStreamDestroy(st);
+    return rc;
+}
+
 extern "C" void *b200_decoder_stream(b200_decoder_t *d) { return d ? d->stream : nullptr; }
 
 extern "C" int b200_decoder_destroy(b200_decoder_t *d) {

@@ -110,7 +110,7 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // Thread-block clusters: this CTA's rank, the address of the same shared
-// variable in CTA `rank` of the cluster, a 16-byte store there, and the
+// variable in CTA `rank` of the cluster, a 16- or 4-byte store there, and the
 // cluster-wide barrier (every thread of every CTA arrives, then waits;
 // release / acquire order the shared-memory writes around it).
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -126,6 +126,9 @@ __device__ __forceinline__ uint32_t cluster_map(const void *local, uint32_t rank
 __device__ __forceinline__ void st_cluster_f4(uint32_t addr, float4 v) {
     asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
                  : "memory");
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");

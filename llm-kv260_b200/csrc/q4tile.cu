@@ -496,12 +496,12 @@ __global__ void __maxnreg__((TileRegs<XMODE, PRO, EPI>::value)) q4_tile_kernel(c
                 }
                 p.y[row] = out;
                 if (row >= k0) {
-                    // K rows [kv head][stride][hd], segments swizzled by position
-                    // (k_swizzled); V transposed, [kv head][hd][stride]
+                    // K rows [kv head][stride][hd], lane-major and swizzled by
+                    // position (k_slot); V transposed, [kv head][hd][stride]
                     const bool isk = row < v0;
                     const int rr = row - (isk ? k0 : v0), st = p.dec.kv_stride;
                     const size_t at =
-                        isk ? (static_cast<size_t>(rr / hd) * st + dpos) * hd + k_swizzled(rr % hd, dpos, p.dec.kv_f16 ? 2 : 4)
+                        isk ? (static_cast<size_t>(rr / hd) * st + dpos) * hd + k_slot(rr % hd, dpos, p.dec.kv_f16 ? 2 : 4, hd)
                             : static_cast<size_t>(rr) * st + dpos;
                     void *cache = isk ? p.dec.kcache : p.dec.vcache;
                     if (p.dec.kv_f16)

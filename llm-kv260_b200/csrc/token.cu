@@ -519,12 +519,12 @@ __device__ void gemv_phase(const MkParams &p, const TokenPhase &ph, const PhaseC
                     }
                     ph.y[row] = out;
                     if (row >= k0) {
-                        // K rows [kv head][stride][hd], segments swizzled by position
-                        // (k_swizzled); V transposed, [kv head][hd][stride]
+                        // K rows [kv head][stride][hd], lane-major and swizzled by
+                        // position (k_slot); V transposed, [kv head][hd][stride]
                         const bool isk = row < v0;
                         const int q = row - (isk ? k0 : v0);
                         const size_t at = isk ? (static_cast<size_t>(q / hd) * a.kv_stride + cx.P) * hd +
-                                                    k_swizzled(q % hd, cx.P, a.kv_f16 ? 2 : 4)
+                                                    k_slot(q % hd, cx.P, a.kv_f16 ? 2 : 4, hd)
                                               : static_cast<size_t>(q) * a.kv_stride + cx.P;
                         void *cache = isk ? ph.kcache : ph.vcache;
                         if (a.kv_f16)

@@ -262,3 +262,17 @@ def test_tensor_parallel_decode_on_n_gpus(cuda_lib, tmp_path, world):
         for mode in ("graph", "persistent"):
             assert res[mode]["forward"] and res[mode]["generate"] and res[mode]["status"] == 0, (mode, res)
         assert res["reference"] and all(v is True for v in res["reference"].values()), res["reference"]
+
+
+@pytest.mark.gpu
+def test_launch_floor(cuda_lib):
+    """The empty-kernel chain that bench.py reports beside the token time:
+    it runs with and without programmatic dependent launch, and refuses bad
+    arguments before launching anything."""
+    import ctypes
+    us = ctypes.c_float(0.0)
+    for smem, pdl in ((0, 1), (200 * 1024, 1), (0, 0)):
+        assert cuda_lib.b200_launch_floor(0, 16, 148, 288, smem, pdl, 10, ctypes.byref(us)) == 0
+        assert 0.0 < us.value < 1000.0
+    assert cuda_lib.b200_launch_floor(0, 0, 148, 288, 0, 1, 10, ctypes.byref(us)) != 0
+    assert cuda_lib.b200_launch_floor(0, 16, 148, 2048, 0, 1, 10, ctypes.byref(us)) != 0
