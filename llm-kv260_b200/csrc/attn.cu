@@ -356,6 +356,7 @@ struct StreamSmem {
     int krows;     // K rows per stage
     int vcol;      // bytes between two V^T columns of a stage (odd number of 16-byte units)
     int vstage;    // bytes of a V^T stage
+    int ptq;       // floats between two lane rows of the lane-major exponentials (= 8 mod 32)
 };
 
 __host__ __device__ inline StreamSmem stream_smem_layout(int d, int esz, int stride) {
@@ -370,8 +371,14 @@ __host__ __device__ inline StreamSmem stream_smem_layout(int d, int esz, int str
         off += (bytes + 15) / 16 * 16;
         return at;
     };
+    // lane rows of the exponentials ptq = 8 (mod 32) floats apart: the four
+    // lanes' stores of 8 consecutive row entries fall on 32 distinct banks
+    // (rows stay 16-byte aligned for the sums' loads)
+    const int q4 = stride / 4;
+    L.ptq = q4 + ((8 - q4 % 32) + 32) % 32;
+    const int lanes_bytes = 16 * L.ptq * 4;
     L.e = carve(16 * stride);
-    L.pt = carve(16 * stride);
+    L.pt = carve(lanes_bytes > 16 * stride ? lanes_bytes : 16 * stride);
     L.ring = carve(kring > vring ? kring : vring);
     L.qs = carve(4 * d * 4);
     L.part = carve((kStreamThreads / 32) * 16);
@@ -543,7 +550,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) attn_stream_kernel(const __
         m[2] = attn_max_gt(m[2], pw.z);
         m[3] = attn_max_gt(m[3], pw.w);
     }
-    const int q4 = p.stride / 4;
+    const int q4 = S.ptq;
     for (int t = tid; t < n; t += NT) {
         float4 sc = e[t];
         sc.x = v_expf(__fsub_rn(sc.x, m[0]));
@@ -569,17 +576,25 @@ __global__ void __launch_bounds__(kStreamThreads, 1) attn_stream_kernel(const __
         const float *row = pt + (4 * b + j4) * q4;
         float acc = 0.0f;
         if (b < G) {
+            // rows are 16-byte aligned (ptq % 4 == 0); each group's four
+            // values are loaded while the previous group's adds run
             int u = 0;
-            const bool al = (q4 & 3) == 0;  // rows 16-byte aligned: q4 % 4 == 0 (stride % 16 == 0)
-            if (al) {
+            if (nu >= 4) {
+                float4 cur = *reinterpret_cast<const float4 *>(row);
 #pragma unroll 4
-                for (; u + 4 <= nu; u += 4) {
-                    const float4 v4 = *reinterpret_cast<const float4 *>(row + u);
-                    acc = __fadd_rn(acc, v4.x);
-                    acc = __fadd_rn(acc, v4.y);
-                    acc = __fadd_rn(acc, v4.z);
-                    acc = __fadd_rn(acc, v4.w);
+                for (; u + 8 <= nu; u += 4) {
+                    const float4 nxt = *reinterpret_cast<const float4 *>(row + u + 4);
+                    acc = __fadd_rn(acc, cur.x);
+                    acc = __fadd_rn(acc, cur.y);
+                    acc = __fadd_rn(acc, cur.z);
+                    acc = __fadd_rn(acc, cur.w);
+                    cur = nxt;
                 }
+                acc = __fadd_rn(acc, cur.x);
+                acc = __fadd_rn(acc, cur.y);
+                acc = __fadd_rn(acc, cur.z);
+                acc = __fadd_rn(acc, cur.w);
+                u += 4;
             }
             for (; u < nu; ++u) acc = __fadd_rn(acc, row[u]);
         }
