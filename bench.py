@@ -501,11 +501,12 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
             "cpu_baseline": cpu,
             "token_check": check,
             "l2_resident": l2_resident,
-            "e2e": {"value": args.steps / wall, "unit": UNIT, "h2d_bytes_per_step": 12,
-                    "d2h_bytes_per_step": 8 + 4 + (4 if world > 1 else 0),
-                    "call": "b200_decoder_forward per token: token, position and prompt length in from pinned host "
-                            "memory (12 B), the pick (8 B) and the status words back, one wait per token; host wall "
-                            "clock around the steps (max over ranks)",
+            "e2e": {"value": args.steps / wall, "unit": UNIT, "h2d_bytes_per_step": 16 if persistent else 12,
+                    "d2h_bytes_per_step": 8 + 4 + 4 + (4 if world > 1 else 0) if persistent else 16,
+                    "call": "b200_decoder_forward per token: one graph launch that copies position, prompt length "
+                            "and token in from pinned host memory (12 B, one copy), runs the token and copies the "
+                            "pick, its logit and the two status words back (16 B, one copy); one wait per token; "
+                            "host wall clock around the steps (max over ranks)",
                     "tokens_same_as_timed_run": e2e_same,
                     "generate_call": {"value": args.steps / gen_wall, "unit": UNIT,
                                       "call": "b200_decoder_generate: the same loop queued, each token copied to "

@@ -53,14 +53,17 @@ struct DecLayer {
 // small device state, one allocation
 struct DevState {
     int pos;
-    int n_prompt;       // next to pos: forward() sets both with one copy
+    int n_prompt;        // pos, n_prompt and in_token: set together by one copy from the host
+    int in_token;        // >= 0: the token at pos (forward's input), which the embedding prologue takes
+                         // instead of tokens[pos] and records there; the token's advance resets it to -1
     unsigned step;
-    int pad;
-    int pick[2];        // the token (int32) and its logit (float32 bits)
-    int pick_local[2];  // several ranks: this rank's pick over its vocab shard
+    int pick[2];         // the token (int32) and its logit (float32 bits)
+    unsigned status[2];  // next to pick: the device and peer status words as the token's advance saw them
+    int pick_local[2];   // several ranks: this rank's pick over its vocab shard
 };
 
-__global__ void advance_kernel(DevState *st, int *tokens, int ctx_max) {
+__global__ void advance_kernel(DevState *st, int *tokens, int ctx_max, const unsigned *status,
+                               const unsigned *peer_status) {
     pdl_launch_dependents();
     pdl_wait_prior_grid();
     // runtime::generate's step (tp_llama.cpp:951-959) on the device
@@ -68,6 +71,9 @@ __global__ void advance_kernel(DevState *st, int *tokens, int ctx_max) {
     if (nx >= st->n_prompt && nx <= ctx_max) tokens[nx] = st->pick[0];
     st->pos = nx;
     st->step += 1u;
+    st->in_token = -1;
+    st->status[0] = *reinterpret_cast<const volatile unsigned *>(status);
+    st->status[1] = peer_status ? *reinterpret_cast<const volatile unsigned *>(peer_status) : 0u;
 }
 
 int dfail(int code, const char *fmt, ...) {
@@ -82,7 +88,7 @@ int dfail(int code, const char *fmt, ...) {
 }  // namespace
 
 namespace {
-constexpr int kIoSlots = 5;  // forward(): token, position, n_prompt, then the status and peer status words
+constexpr int kIoSlots = 8;  // forward(): position, n_prompt, token; then pick, value, status, peer status
 }  // namespace
 
 struct b200_decoder {
@@ -105,9 +111,11 @@ struct b200_decoder {
     bool output_set;
     cudaGraphExec_t graph;   // one token
     cudaGraphExec_t graphk;  // kGraphTokens tokens in a row: dependent launches overlap across token boundaries too
+    cudaGraphExec_t fwd;     // forward(): the input copy, one token, the output copy
     int host_pos;       // where the device loop stands after the work queued so far
     int32_t *host_io;   // pinned, mapped: [0, 2) the pick, [2, 2 + ctx_max + 1) token ids by position, then
-                        // kIoSlots words for forward(): token, position, n_prompt in; status words out
+                        // kIoSlots words for forward(): position, n_prompt, token in; pick, value, status
+                        // words out
     Tuning tu;
     // persistent mode
     bool persistent;
@@ -207,6 +215,7 @@ void norm_prologue(const b200_decoder_t *d, TileLaunch &L, int pro, const float 
     L.dec.exact_norm = d->c.exact_norm;
     L.dec.embd = d->token_embd;
     L.dec.tokens = d->tokens;
+    L.dec.in_token = pro == kProEmbedNorm ? &d->st->in_token : nullptr;
     L.dec.pos = &d->st->pos;
 }
 
@@ -308,6 +317,8 @@ int enqueue_token(b200_decoder_t *d) {
         H.dec.adv_tokens = d->tokens;
         H.dec.n_prompt = &d->st->n_prompt;
         H.dec.ctx_max = c.ctx_max;
+        H.dec.adv_in_token = &d->st->in_token;
+        H.dec.adv_status = d->st->status;
     }
     H.trace = launch_trace(d, 5 * c.n_layer);
     if (int rc = launch(d, H, "lm_head")) return rc;
@@ -324,7 +335,8 @@ int enqueue_token(b200_decoder_t *d) {
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        if (cudaLaunchKernelEx(&cfg, advance_kernel, d->st, d->tokens, c.ctx_max) != cudaSuccess)
+        if (cudaLaunchKernelEx(&cfg, advance_kernel, d->st, d->tokens, c.ctx_max, static_cast<const unsigned *>(status_word()),
+                               static_cast<const unsigned *>(d->peer_status)) != cudaSuccess)
             return dfail(kErrCuda, "decoder: advance launch failed");
     }
     return 0;
@@ -476,7 +488,8 @@ int capture_tokens(b200_decoder_t *d, int tokens, cudaGraphExec_t *out) {
 void drop_graphs(b200_decoder_t *d) {
     if (d->graph) cudaGraphExecDestroy(d->graph);
     if (d->graphk) cudaGraphExecDestroy(d->graphk);
-    d->graph = d->graphk = nullptr;
+    if (d->fwd) cudaGraphExecDestroy(d->fwd);
+    d->graph = d->graphk = d->fwd = nullptr;
 }
 
 int ready(b200_decoder_t *d) {
@@ -499,8 +512,8 @@ int ready(b200_decoder_t *d) {
 // The loop's position and prompt length, written on the decoder's stream
 // (the step counter stays as the device left it: the ranks' epochs follow it).
 int set_state(b200_decoder_t *d, int pos, int n_prompt) {
-    if (int rc = h2d(&d->st->pos, &pos, 4, d->stream)) return rc;
-    if (int rc = h2d(&d->st->n_prompt, &n_prompt, 4, d->stream)) return rc;
+    const int v[3] = {pos, n_prompt, -1};  // pos, n_prompt, in_token
+    if (int rc = h2d(&d->st->pos, v, sizeof v, d->stream)) return rc;
     d->host_pos = pos;
     return 0;
 }
@@ -749,6 +762,35 @@ extern "C" int b200_decoder_set_output(b200_decoder_t *d, const void *token_embd
     return 0;
 }
 
+namespace {
+// forward()'s graph (graph mode): the inputs {pos, n_prompt, in_token} from
+// pinned host memory into the device state in one copy, the token's kernels
+// (the embedding prologue takes in_token), and {pick, value, status, peer
+// status} back in one copy -- one launch and one wait per call.
+int forward_graph(b200_decoder_t *d) {
+    if (d->fwd) return 0;
+    static_assert(offsetof(DevState, n_prompt) == offsetof(DevState, pos) + 4 &&
+                      offsetof(DevState, in_token) == offsetof(DevState, pos) + 8,
+                  "pos, n_prompt and in_token adjacent");
+    static_assert(offsetof(DevState, status) == offsetof(DevState, pick) + 8, "pick and the status words adjacent");
+    int32_t *in = d->host_io + 3 + d->c.ctx_max, *out = in + 4;
+    cudaGraph_t g = nullptr;
+    if (cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeRelaxed) != cudaSuccess)
+        return dfail(kErrCuda, "decoder: capture failed: %s", cudaGetErrorString(cudaGetLastError()));
+    cudaError_t e = cudaMemcpyAsync(&d->st->pos, in, 12, cudaMemcpyHostToDevice, d->stream);
+    const int rc = e == cudaSuccess ? enqueue_token(d) : kErrCuda;
+    if (!rc) e = cudaMemcpyAsync(out, d->st->pick, 16, cudaMemcpyDeviceToHost, d->stream);
+    const cudaError_t ee = cudaStreamEndCapture(d->stream, &g);
+    if (rc || e != cudaSuccess || ee != cudaSuccess || cudaGraphInstantiate(&d->fwd, g, 0) != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        d->fwd = nullptr;
+        return dfail(rc ? rc : kErrCuda, "decoder: forward graph failed: %s", cudaGetErrorString(cudaGetLastError()));
+    }
+    cudaGraphDestroy(g);
+    return 0;
+}
+}  // namespace
+
 extern "C" int b200_decoder_forward(b200_decoder_t *d, int token, int pos, int32_t *pick, float *value) {
     if (int rc = ready(d)) return rc;
     if (token < 0 || token >= d->c.n_vocab || pos < 0 || pos >= d->c.ctx_max)
@@ -758,27 +800,35 @@ extern "C" int b200_decoder_forward(b200_decoder_t *d, int token, int pos, int32
     // (prefill / step) finishes first, so the pinned words are free.
     if (cudaStreamSynchronize(d->stream) != cudaSuccess)
         return dfail(kErrCuda, "decoder: stream failed: %s", cudaGetErrorString(cudaGetLastError()));
-    int32_t *io = d->host_io + 3 + d->c.ctx_max;  // kIoSlots words
-    io[0] = token;
-    io[1] = pos;
-    io[2] = INT_MAX;  // n_prompt: the loop's advance writes no token
-    io[3] = io[4] = 0;
-    static_assert(offsetof(DevState, n_prompt) == offsetof(DevState, pos) + 4, "pos and n_prompt adjacent");
-    cudaError_t e = cudaMemcpyAsync(d->tokens + pos, io, 4, cudaMemcpyHostToDevice, d->stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(&d->st->pos, io + 1, 8, cudaMemcpyHostToDevice, d->stream);
-    if (e != cudaSuccess) return dfail(kErrCuda, "decoder: copy to the device failed: %s", cudaGetErrorString(e));
-    d->host_pos = pos;
-    if (int rc = launch_steps(d, 1)) return rc;
-    e = cudaMemcpyAsync(d->host_io, d->st->pick, 8, cudaMemcpyDeviceToHost, d->stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(io + 3, status_word(), 4, cudaMemcpyDeviceToHost, d->stream);
-    if (e == cudaSuccess && d->peer_status) e = cudaMemcpyAsync(io + 4, d->peer_status, 4, cudaMemcpyDeviceToHost, d->stream);
+    int32_t *in = d->host_io + 3 + d->c.ctx_max, *out = in + 4;  // kIoSlots words
+    in[0] = pos;
+    in[1] = INT_MAX;  // n_prompt: the loop's advance writes no token
+    cudaError_t e = cudaSuccess;
+    if (!d->persistent) {
+        if (int rc = forward_graph(d)) return rc;
+        in[2] = token;  // in_token: the embedding prologue takes it and records it at tokens[pos]
+        out[2] = out[3] = 0;
+        e = cudaGraphLaunch(d->fwd, d->stream);
+        d->host_pos = pos + 1;
+    } else {
+        // the persistent kernel reads the token from tokens[pos]
+        in[2] = -1;
+        in[3] = token;
+        e = cudaMemcpyAsync(d->tokens + pos, in + 3, 4, cudaMemcpyHostToDevice, d->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(&d->st->pos, in, 12, cudaMemcpyHostToDevice, d->stream);
+        if (e != cudaSuccess) return dfail(kErrCuda, "decoder: copy to the device failed: %s", cudaGetErrorString(e));
+        d->host_pos = pos;
+        if (int rc = launch_steps(d, 1)) return rc;
+        e = cudaMemcpyAsync(out, d->st->pick, 8, cudaMemcpyDeviceToHost, d->stream);
+        out[2] = out[3] = 1;  // the full status check below (and the persistent kernel's abort flag)
+    }
     if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
     if (e != cudaSuccess) return dfail(kErrCuda, "decoder: forward failed: %s", cudaGetErrorString(e));
-    if (io[3] || io[4] || d->persistent) {
-        if (int rc = check_status(d)) return rc;  // the full check (and the persistent kernel's abort flag)
+    if (out[2] || out[3]) {
+        if (int rc = check_status(d)) return rc;  // the full check
     }
-    if (pick) *pick = d->host_io[0];
-    if (value) memcpy(value, &d->host_io[1], 4);
+    if (pick) *pick = out[0];
+    if (value) memcpy(value, &out[1], 4);
     return 0;
 }
 

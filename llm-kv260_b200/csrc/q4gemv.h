@@ -124,6 +124,8 @@ struct DecodeOps {
     int exact_norm = 0;                // 1: always sum the squares in the reference's order
     const uint8_t *embd = nullptr;     // token_embd, GGUF Q4_0 rows [n_vocab][k/32*18]
     const int *tokens = nullptr;       // token id by position
+    int *in_token = nullptr;           // optional (embedding prologue): >= 0 is the token at pos, taken instead
+                                       // of tokens[pos] and recorded there by CTA 0
     const int *pos = nullptr;          // the current position (device)
     const float *rope_cs = nullptr;    // [ctx_max][head_dim]: cos, sin of pair i at 2i, 2i+1
     int head_dim = 0, q_rows = 0, kv_rows = 0, ctx_max = 0, kv_f16 = 1;
@@ -144,6 +146,9 @@ struct DecodeOps {
     unsigned *adv_step = nullptr;
     int *adv_tokens = nullptr;         // tokens[pos + 1] = the pick when pos + 1 >= *n_prompt
     const int *n_prompt = nullptr;
+    int *adv_in_token = nullptr;       // optional: reset to -1 by the advance
+    unsigned *adv_status = nullptr;    // optional: [0] the status word, [1] the peer status word (0 without
+                                       // one), as the advance sees them
 };
 
 struct TileLaunch {

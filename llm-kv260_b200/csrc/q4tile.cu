@@ -141,7 +141,9 @@ __device__ __forceinline__ void stage_x_f32(const TileParams &p, uint8_t *xs, fl
     for (int j = 0; j < E; ++j) v[j] = 0.0f;
     if (live) {
         if (pro == kProEmbedNorm) {
-            const int tok = p.dec.tokens[*p.dec.pos];
+            const int at = *p.dec.pos, given = p.dec.in_token ? *p.dec.in_token : -1;
+            const int tok = given >= 0 ? given : p.dec.tokens[at];
+            if (given >= 0 && blockIdx.x == 0 && threadIdx.x == 0) const_cast<int *>(p.dec.tokens)[at] = given;
             const uint8_t *blk = p.dec.embd + (static_cast<size_t>(tok) * nb + b) * kBlockBytes;
             const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(blk)));
 #pragma unroll
@@ -603,6 +605,13 @@ __global__ void __maxnreg__((TileRegs<XMODE, PRO, EPI>::value)) q4_tile_kernel(c
         named_sync(1, kConsumers);
         if (s_last && t < 32) {
             __threadfence();
+            // the status words for the advance's record, loaded here so their
+            // latency passes under the candidates' reduction
+            unsigned st0 = 0u, st1 = 0u;
+            if (t == 0 && p.dec.adv_status) {
+                st0 = *reinterpret_cast<volatile unsigned *>(p.status);
+                if (p.dec.peer_status) st1 = *reinterpret_cast<volatile unsigned *>(p.dec.peer_status);
+            }
             float bv = __int_as_float(0x7fc00000);
             int bi = 0x7fffffff;
             for (int c = t; c < static_cast<int>(gridDim.x); c += 32) {
@@ -636,6 +645,11 @@ __global__ void __maxnreg__((TileRegs<XMODE, PRO, EPI>::value)) q4_tile_kernel(c
                     if (nx >= *p.dec.n_prompt && nx <= p.dec.ctx_max) p.dec.adv_tokens[nx] = bi + p.sel_base;
                     *p.dec.adv_pos = nx;
                     *p.dec.adv_step += 1u;
+                    if (p.dec.adv_in_token) *p.dec.adv_in_token = -1;
+                    if (p.dec.adv_status) {
+                        p.dec.adv_status[0] = st0;
+                        p.dec.adv_status[1] = st1;
+                    }
                 }
             }
         }
