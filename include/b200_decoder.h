@@ -81,7 +81,10 @@ B200_API int b200_decoder_set_layer(b200_decoder_t *d, int layer, const void *at
 B200_API int b200_decoder_set_output(b200_decoder_t *d, const void *token_embd, const float *output_norm);
 
 /* runtime::forward(token, pos) then the greedy pick over all ranks: *pick is
- * the token, *value its logit. Every rank must make the same calls. */
+ * the token, *value its logit. Every rank must make the same calls. Waits
+ * for work queued earlier, then (graph mode) launches one CUDA graph -- the
+ * inputs in, the token, the pick and status words out -- and waits for it;
+ * the first call captures that graph. */
 B200_API int b200_decoder_forward(b200_decoder_t *d, int token, int pos, int32_t *pick, float *value);
 
 /* The same loop, queued without waiting (for callers that time or overlap
