@@ -486,7 +486,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                        "prompt": n_prompt, "positions": [n_prompt + args.warmup, n_prompt + args.warmup + args.steps],
                        "parallelism": f"tp{world}", "weight_bytes_per_rank": weight_bytes,
                        "mode": args.mode + (" (one cooperative kernel per run of tokens)" if persistent
-                                            else " (a CUDA graph of 81 kernels per token)"),
+                                            else f" (CUDA graphs, {kernels_per_token} kernels per token)"),
                        "l2": ("flushed before every step (per-rank weights smaller than L2)" if flush_needed
                               else "per-rank weights larger than L2, no flush")},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
