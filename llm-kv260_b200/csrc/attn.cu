@@ -332,14 +332,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
     }
 }
 
-// Long contexts, cluster form: the cluster kernel's split (CTA r scores a
-// quarter of the positions and chains a quarter of the columns) with K and
-// V^T streamed through rings of shared-memory stages instead of held whole.
+// Long contexts, cluster form: the cluster kernel's split over kStreamSplit
+// CTAs per KV head (CTA r scores an eighth of the positions and chains an
+// eighth of the columns) with K and V^T streamed through rings of
+// shared-memory stages instead of held whole.
 //   scores  4 threads per position (fused-multiply-add lane j each: q's
 //           elements j, j+4, ... of every head in registers, the lane's
 //           quarter of the lane-major K row from the ring; met by xor
 //           shuffles 1 then 2: vaddvq_f32's pairing); every score row to all
-//           four CTAs (distributed shared memory); one cluster barrier;
+//           the cluster's CTAs (distributed shared memory); one cluster
+//           barrier;
 //   softmax each CTA: maxima, v_expf, the four sequential lane sums per head
 //           read from a lane-major copy of the exponentials, 1 / sum, p;
 //   output  one thread per (column, head): the fused-multiply-add chain over
@@ -347,6 +349,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_kernel(const __grid_cons
 // The V^T ring reuses the K ring's shared memory and starts filling as soon
 // as the scores are done, behind the softmax.
 constexpr int kStreamThreads = 256;
+constexpr int kStreamSplit = 8;  // CTAs per KV head at long contexts: the cluster size (the portable maximum)
 constexpr int kStreamKStages = 4;
 constexpr int kStreamVStages = 3;
 constexpr int kStreamColBytes = 512;  // V^T bytes of a column per stage
@@ -363,7 +366,7 @@ __host__ __device__ inline StreamSmem stream_smem_layout(int d, int esz, int str
     StreamSmem L{};
     L.krows = 16384 / (d * esz);  // 16 KB per K stage
     L.vcol = kStreamColBytes + 16;
-    L.vstage = (d / kSplit) * L.vcol;
+    L.vstage = (d / kStreamSplit) * L.vcol;
     const int kring = kStreamKStages * L.krows * d * esz, vring = kStreamVStages * L.vstage;
     int off = 0;
     auto carve = [&](int bytes) {
@@ -392,7 +395,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) attn_stream_kernel(const __
     constexpr int kRowBytes = D * ESZ;
     constexpr int kSegs = kRowBytes / 16;
     constexpr int kPer = 16 / ESZ;
-    constexpr int CW = D / kSplit;
+    constexpr int CW = D / kStreamSplit;
     constexpr int kChunkPos = kStreamColBytes / ESZ;  // positions per V^T stage
     constexpr int NT = kStreamThreads;
     constexpr int kQv = (4 * D + NT - 1) / NT;
@@ -408,7 +411,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) attn_stream_kernel(const __
     float *part = reinterpret_cast<float *>(smem + S.part);
     float *hinv = reinterpret_cast<float *>(smem + S.hinv);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, G = p.group, KC = S.krows;
-    const int kvh = blockIdx.x / kSplit;
+    const int kvh = blockIdx.x / kStreamSplit;
     const int r = static_cast<int>(cluster_ctarank());
     const int c0 = r * CW;
     const size_t head_bytes = static_cast<size_t>(p.stride) * D * ESZ;
@@ -429,7 +432,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) attn_stream_kernel(const __
     attn_stamp_at(rec, 1);
 
     const int n = *p.pos + 1;
-    const int per = (n + kSplit - 1) / kSplit;
+    const int per = (n + kStreamSplit - 1) / kStreamSplit;
     const int r0 = min(n, r * per), r1 = min(n, r0 + per);
     const int nk = (r1 - r0 + KC - 1) / KC;
     const int nv = (n + kChunkPos - 1) / kChunkPos;
@@ -511,8 +514,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) attn_stream_kernel(const __
                 const float x = __fadd_rn(acc[b], __shfl_xor_sync(kFullMask, acc[b], 1));
                 if (b < G) sv[b] = __fmul_rn(__fadd_rn(x, __shfl_xor_sync(kFullMask, x, 2)), p.scale);
             }
-            if (live && jl < kSplit)  // the four lanes hold the same row: lane j writes CTA j's copy
-                st_cluster_f4(cluster_map(&e[t], static_cast<uint32_t>(jl)), make_float4(sv[0], sv[1], sv[2], sv[3]));
+            if (live)  // the four lanes hold the same row: lane j writes the copies of CTAs j, j + 4, ...
+                for (int q = jl; q < kStreamSplit; q += 4)
+                    st_cluster_f4(cluster_map(&e[t], static_cast<uint32_t>(q)), make_float4(sv[0], sv[1], sv[2], sv[3]));
         }
         __syncthreads();  // stage consumed
         if (tid == 0) stage_k(kc + kStreamKStages);
@@ -722,13 +726,14 @@ int attn_launch(const AttnLaunch &L, cudaStream_t stream) {
     p.scale = L.scale;
     p.trace = L.trace;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(L.kvh_local * kSplit);
+    const int split = long_ctx ? kStreamSplit : kSplit;
+    cfg.gridDim = dim3(L.kvh_local * split);
     cfg.blockDim = dim3(long_ctx ? kStreamThreads : kAttnThreads);
     cfg.dynamicSmemBytes = static_cast<size_t>(smem);
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;  // kSplit CTAs of one KV head, scheduled together
-    attr[0].val.clusterDim.x = kSplit;
+    attr[0].id = cudaLaunchAttributeClusterDimension;  // the CTAs of one KV head, scheduled together
+    attr[0].val.clusterDim.x = split;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
